@@ -1,0 +1,442 @@
+"""Benchmark of the fused-RoPE causal attention hot path on B200.
+
+One JSON line on rank 0. Headline: causal bf16 prefill TFLOP/s on the MHA sweep's largest
+configuration (B=2, H=Hkv=32, S=2048, D=64, RoPE base 1e4); a step is one
+``dominus_ultra_prefill`` call over one batch. A secondary ``decode`` object reports the decode
+sweep's largest configuration (B=8, H=Hkv=32, cache L=2048, D=64) in KV-cache HBM GB/s.
+
+* ``value``: device time (CUDA events, max over ranks) with inputs resident in HBM. Each step
+  reads a different one of several input sets whose total exceeds the 126 MB L2, so every step
+  streams from HBM (``config.l2``).
+* ``e2e``: the same metric through the public API with pinned host buffers: host->device copy
+  of q/k/v, the call, and a device->host read of out/lse inside the timed region.
+* ``roofline``: algorithmic FLOPs (4*B*H*D*S(S+1)/2) per launch over the kernel's mean launch
+  time, against the measured dense bf16 peak (``MEASURED_PEAKS.json``).
+* ``cpu_baseline``: the fp32 torch reference path (RoPE then SDPA, the reference's oracle) on
+  the host cores, rank 0 only.
+* Multi-GPU (torchrun): weak scaling; every rank runs the per-GPU workload on its own
+  (batch, kv-head) units with no communication, time = max over ranks.
+
+``--impl reference`` times the reference's CPU path (the oracle port) on the same config.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+PREFILL = dict(B=2, H=32, Hkv=32, S=2048, D=64, base=10000.0)
+DECODE = dict(B=8, H=32, Hkv=32, L=2048, D=64, base=10000.0)
+
+# Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) from the ncu captures
+# summarised under profiles/ (None until captured for the current kernel version).
+NCU_TRAFFIC = {"prefill": None, "decode": None}
+
+
+def prefill_flops(B, H, S, D):
+    return 4.0 * B * H * D * S * (S + 1) / 2.0
+
+
+def decode_bytes(B, H, Hkv, L, D):
+    return 2.0 * B * Hkv * L * D * 2 + 2.0 * B * H * D * 2 + 2.0 * (L + 1) * (D // 2) * 2
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while the timed region runs."""
+
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        self.period = period_s
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._h = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # NVML unavailable: report no clocks
+            self._nv = None
+
+    _REASONS = {
+        "hw_slowdown": 0x8,
+        "sw_thermal_slowdown": 0x20,
+        "hw_thermal_slowdown": 0x40,
+        "hw_power_brake_slowdown": 0x80,
+        "sw_power_cap": 0x4,
+    }
+
+    def _sample(self):
+        nv = self._nv
+        self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+        mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+        for name, bit in self._REASONS.items():
+            if mask & bit:
+                self.reasons.add(name)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self._sample()
+            except Exception:
+                return
+            time.sleep(self.period)
+
+    def start(self):
+        if self._nv is None:
+            return
+        self._sample()
+        self._thread = threading.Thread(target=self._run, daemon=True)
+        self._thread.start()
+
+    def stop(self):
+        if self._nv is None:
+            return None
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+        try:
+            self._sample()
+        except Exception:
+            pass
+        return {
+            "sm_mhz": statistics.median(self.samples) if self.samples else None,
+            "sm_max_mhz": self.max_mhz,
+            "reasons": sorted(self.reasons),
+            "samples": len(self.samples),
+        }
+
+
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+        return dist, dist.get_rank(), world, local
+    return None, 0, 1, 0
+
+
+def barrier(dist):
+    if dist is not None:
+        dist.barrier()
+
+
+def max_over_ranks(dist, value: float, device) -> float:
+    if dist is None:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def make_prefill_sets(cfg, n_sets, seed, device, dtype=torch.bfloat16):
+    from dominusultra_b200 import precompute_rope_cos_sin
+
+    B, H, Hkv, S, D = cfg["B"], cfg["H"], cfg["Hkv"], cfg["S"], cfg["D"]
+    g = torch.Generator(device=device).manual_seed(seed)
+    sets = []
+    for _ in range(n_sets):
+        q = torch.randn(B, H, S, D, generator=g, device=device, dtype=torch.float32).to(dtype)
+        k = torch.randn(B, Hkv, S, D, generator=g, device=device, dtype=torch.float32).to(dtype)
+        v = torch.randn(B, Hkv, S, D, generator=g, device=device, dtype=torch.float32).to(dtype)
+        sets.append((q, k, v))
+    cos, sin = precompute_rope_cos_sin(S, D, device, dtype, cfg["base"])
+    return sets, cos, sin
+
+
+def time_region(fn, steps, stream):
+    """Events around exactly `steps` calls of fn(i) on `stream`; returns total ms."""
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(steps):
+        fn(i)
+    end.record(stream)
+    end.synchronize()
+    return start.elapsed_time(end)
+
+
+def time_launches(fn, steps, stream):
+    """Mean per-launch time: an event pair around each call."""
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for i in range(steps):
+        evs[i][0].record(stream)
+        fn(i)
+        evs[i][1].record(stream)
+    torch.cuda.synchronize()
+    return statistics.mean(a.elapsed_time(b) for a, b in evs)
+
+
+def cpu_prefill_baseline(cfg, reps=3):
+    """fp32 torch reference path on the host cores (RoPE then SDPA per head block)."""
+    import oracle
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    B, H, Hkv, S, D = cfg["B"], cfg["H"], cfg["Hkv"], cfg["S"], cfg["D"]
+    g = torch.Generator().manual_seed(7)
+    q = torch.randn(B, H, S, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, Hkv, S, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, Hkv, S, D, generator=g).to(torch.bfloat16)
+    cos, sin = oracle.precompute_rope_cos_sin(S, D, torch.bfloat16, cfg["base"])
+
+    def run():
+        qr = oracle.apply_rope(q, cos, sin)
+        kr = oracle.apply_rope(k, cos, sin).repeat_interleave(H // Hkv, dim=1)
+        return torch.nn.functional.scaled_dot_product_attention(
+            qr, kr, v.float().repeat_interleave(H // Hkv, dim=1), is_causal=True)
+
+    run()
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return prefill_flops(B, H, S, D) / t / 1e12, t, torch.get_num_threads()
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU path (fp32 torch RoPE + SDPA) on the host cores."""
+    dist_rank = int(os.environ.get("RANK", "0"))
+    if dist_rank != 0:
+        return 0
+    cfg = PREFILL
+    tf, t, cores = cpu_prefill_baseline(cfg, reps=1)
+    times = []
+    for _ in range(args.warmup):
+        cpu_prefill_baseline(cfg, reps=1)
+    for _ in range(args.steps):
+        _, ts, _ = cpu_prefill_baseline(cfg, reps=1)
+        times.append(ts)
+    ms = 1000.0 * statistics.mean(times)
+    flops = prefill_flops(cfg["B"], cfg["H"], cfg["S"], cfg["D"])
+    value = flops / (ms / 1000.0) / 1e12
+    line = {
+        "impl": "reference",
+        "metric": "causal prefill TFLOP/s per B200 (decode KV-cache HBM GB/s in 'decode')",
+        "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1), seeded",
+        "config": {"workload": "prefill B2 H32 Hkv32 S2048 D64 causal RoPE base 1e4",
+                   "impl_path": "fp32 torch RoPE then scaled_dot_product_attention on CPU"},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                         "sample": "full workload per step (one prefill of the config)"},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def bench_decode(rank, device, stream, steps, warmup, peaks):
+    from dominusultra_b200 import dominus_ultra_decode, precompute_rope_cos_sin
+
+    c = DECODE
+    B, H, Hkv, L, D = c["B"], c["H"], c["Hkv"], c["L"], c["D"]
+    per_set = 2 * B * Hkv * L * D * 2
+    n_sets = max(2, math.ceil(2 * L2_BYTES / per_set))
+    g = torch.Generator(device=device).manual_seed(1000 + rank)
+    sets = []
+    for _ in range(n_sets):
+        q = torch.randn(B, H, 1, D, generator=g, device=device).to(torch.bfloat16)
+        k = torch.randn(B, Hkv, L, D, generator=g, device=device).to(torch.bfloat16)
+        v = torch.randn(B, Hkv, L, D, generator=g, device=device).to(torch.bfloat16)
+        sets.append((q, k, v))
+    cos, sin = precompute_rope_cos_sin(L + 1, D, device, torch.bfloat16, c["base"])
+
+    def step(i):
+        q, k, v = sets[i % n_sets]
+        dominus_ultra_decode(q, k, v, cos, sin, Hkv)
+
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    ms_total = time_region(step, steps, stream)
+    per_launch_ms = time_launches(step, steps, stream)
+    nbytes = decode_bytes(B, H, Hkv, L, D)
+    gbs = nbytes / (ms_total / steps / 1000.0) / 1e9
+    achieved = nbytes / (per_launch_ms / 1000.0) / 1e9
+    from dominusultra_b200 import _lib
+
+    splits_ws = int(_lib.load().du_decode_workspace_size(B, H, Hkv, L, D))
+    return {
+        "metric": "decode KV-cache HBM GB/s per B200",
+        "value": gbs, "unit": "GB/s", "ms_per_step": ms_total / steps,
+        "config": {"workload": f"decode B{B} H{H} Hkv{Hkv} L{L} D{D} bf16 RoPE base 1e4",
+                   "l2": f"{n_sets} rotating input sets of {per_set / 1e6:.0f} MB (> L2)"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / peaks["hbm_gbs"], "traffic": NCU_TRAFFIC["decode"],
+                     "algorithmic_bytes": nbytes,
+                     "launches_per_step": 2 if splits_ws > 0 else 1},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    if args.impl == "reference":
+        return run_reference(args)
+
+    from dominusultra_b200 import _lib, dominus_ultra_prefill
+
+    dist, rank, world, local = dist_setup(args.gpus)
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    stream = torch.cuda.current_stream(device)
+    peaks, peak_kind = load_peaks()
+    _lib.load()
+
+    cfg = PREFILL
+    B, H, Hkv, S, D = cfg["B"], cfg["H"], cfg["Hkv"], cfg["S"], cfg["D"]
+    per_set = (B * H * S * D + 2 * B * Hkv * S * D) * 2
+    n_sets = max(2, math.ceil(2 * L2_BYTES / per_set))
+    sets, cos, sin = make_prefill_sets(cfg, n_sets, 1234 + rank, device)
+
+    def step(i):
+        q, k, v = sets[i % n_sets]
+        dominus_ultra_prefill(q, k, v, cos, sin, Hkv)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(device.index)
+    barrier(dist)
+    torch.cuda.synchronize()
+    sampler.start()
+    ms_total = time_region(step, args.steps, stream)
+    torch.cuda.synchronize()
+    barrier(dist)
+    clocks = sampler.stop()
+    ms_total = max_over_ranks(dist, ms_total, device)
+    ms_step = ms_total / args.steps
+    flops = prefill_flops(B, H, S, D)
+    value = world * flops / (ms_step / 1000.0) / 1e12
+
+    per_launch_ms = time_launches(step, args.steps, stream)
+    achieved = flops / (per_launch_ms / 1000.0) / 1e12
+
+    # End to end through the public API with pinned host buffers.
+    host_sets = [tuple(t.cpu().pin_memory() for t in s) for s in sets[:2]]
+    q0, k0, v0 = sets[0]
+    out_h = torch.empty(q0.shape, dtype=q0.dtype).pin_memory()
+    lse_h = torch.empty((B, H, S), dtype=torch.float32).pin_memory()
+
+    def e2e_step(i):
+        qh, kh, vh = host_sets[i % 2]
+        q = qh.to(device, non_blocking=True)
+        k = kh.to(device, non_blocking=True)
+        v = vh.to(device, non_blocking=True)
+        out, lse = dominus_ultra_prefill(q, k, v, cos, sin, Hkv)
+        out_h.copy_(out, non_blocking=True)
+        lse_h.copy_(lse, non_blocking=True)
+
+    for i in range(2):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    barrier(dist)
+    e2e_ms = time_region(e2e_step, args.steps, stream) / args.steps
+    e2e_ms = max_over_ranks(dist, e2e_ms, device)
+    h2d = sum(t.numel() * t.element_size() for t in host_sets[0])
+    d2h = out_h.numel() * out_h.element_size() + lse_h.numel() * 4
+
+    decode = None
+    if not args.no_decode:
+        decode = bench_decode(rank, device, stream, args.steps, args.warmup, peaks)
+        if dist is not None:
+            dms = max_over_ranks(dist, decode["ms_per_step"], device)
+            decode["ms_per_step"] = dms
+            decode["value"] = world * decode_bytes(DECODE["B"], DECODE["H"], DECODE["Hkv"],
+                                                   DECODE["L"], DECODE["D"]) / (dms / 1000.0) / 1e9
+
+    status = _lib.read_status(reset=True)
+    line = None
+    if rank == 0:
+        peak = peaks["bf16_tflops"]
+        line = {
+            "metric": "causal prefill TFLOP/s per B200 (decode KV-cache HBM GB/s in 'decode')",
+            "value": value,
+            "unit": "TFLOP/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms_step,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic N(0,1) bf16, seeded per rank; RoPE tables from precompute_rope_cos_sin",
+            "config": {
+                "workload": f"prefill B{B} H{H} Hkv{Hkv} S{S} D{D} causal RoPE base 1e4 (per GPU)",
+                "parallelism": f"(batch, kv-head) units sharded over {world} GPU(s), no communication",
+                "l2": f"{n_sets} rotating input sets of {per_set / 1e6:.0f} MB (> L2)",
+            },
+            "roofline": {
+                "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak, "traffic": NCU_TRAFFIC["prefill"],
+                "peak_kind": f"{peak_kind} bf16 dense (burst)",
+                "algorithmic_flops": flops,
+            },
+            "e2e": {"value": world * flops / (e2e_ms / 1000.0) / 1e12, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+            "device_status": status,
+        }
+        if decode is not None:
+            line["decode"] = decode
+        if not args.no_cpu_baseline:
+            tf, t, cores = cpu_prefill_baseline(cfg)
+            line["cpu_baseline"] = {
+                "value": tf, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                "sample": f"full workload (one prefill of the config), median of 3, {t * 1000:.0f} ms each",
+            }
+        print(json.dumps(line))
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

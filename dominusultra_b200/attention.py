@@ -1,0 +1,333 @@
+"""Drop-in Python API of DominusUltra's fused-RoPE attention, backed by sm_100a CUDA.
+
+Same names, signatures, argument meaning, validation order and error messages as the reference
+module ``dominus_ultra.py``; the Triton launches are replaced by calls into the C ABI of
+``libdominus_b200.so`` (``include/dominus_ultra_b200.h``). Launches go to torch's current
+stream of the tensors' device and return without synchronising, like the reference.
+There is no CPU path: CPU tensors are rejected exactly as the reference rejects them.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Sequence, Tuple
+
+import torch
+
+from . import _lib
+
+__all__ = [
+    "precompute_rope_cos_sin",
+    "dominus_ultra_prefill",
+    "dominus_ultra_decode",
+    "decode_partial",
+    "merge_partials",
+]
+
+
+def precompute_rope_cos_sin(
+    max_seq_len: int, dim: int, device, dtype=torch.float32, base: float = 10000.0
+) -> Tuple[torch.Tensor, torch.Tensor]:
+    """
+    Pre-compute RoPE (Rotary Position Embedding) cos/sin values.
+
+    Same contract as the reference (``dominus_ultra.py:25-58``): returns ``(cos, sin)``, each
+    ``[max_seq_len, dim // 2]``, computed in fp32 as ``cos/sin(t * base ** (-2j / dim))`` and
+    cast to ``dtype``; bit-identical to the reference on CPU. Runs on any device.
+    """
+    if max_seq_len <= 0:
+        raise ValueError("max_seq_len must be positive")
+    if dim <= 0 or dim % 2 != 0:
+        raise ValueError("dim must be a positive even integer")
+    if base <= 0:
+        raise ValueError("base must be positive")
+
+    inv_freq = 1.0 / (
+        base ** (torch.arange(0, dim, 2, device=device, dtype=torch.float32) / dim)
+    )
+    t = torch.arange(max_seq_len, device=device, dtype=torch.float32)
+    freqs = torch.einsum("i,j->ij", t, inv_freq)
+    return freqs.cos().to(dtype), freqs.sin().to(dtype)
+
+
+def _validate_head_dim(head_dim: int) -> None:
+    # dominus_ultra.py:70-72
+    if head_dim < 16 or head_dim > 256 or head_dim & (head_dim - 1):
+        raise ValueError("head_dim must be a power of two between 16 and 256")
+
+
+def _validate_rope_tables(
+    cos: torch.Tensor,
+    sin: torch.Tensor,
+    positions: int,
+    head_dim: int,
+    device: torch.device,
+    dtype: torch.dtype,
+) -> None:
+    # dominus_ultra.py:75-101
+    expected_tail = (head_dim // 2,)
+    if cos.ndim != 2 or sin.ndim != 2:
+        raise ValueError("cos and sin must be rank-2 [positions, head_dim // 2] tensors")
+    if cos.shape[0] < positions or sin.shape[0] < positions:
+        raise ValueError(f"cos and sin must contain at least {positions} positions")
+    if cos.shape[1:] != expected_tail or sin.shape[1:] != expected_tail:
+        raise ValueError(f"cos and sin must have trailing shape {expected_tail}")
+    if cos.device != device or sin.device != device:
+        raise ValueError("cos and sin must be on the same device as the attention tensors")
+    if cos.dtype != dtype or sin.dtype != dtype:
+        raise ValueError("cos and sin must have the same dtype as the attention tensors")
+    if not cos.is_contiguous() or not sin.is_contiguous():
+        raise ValueError("cos and sin must be contiguous")
+
+
+def _validate_attention_tensors(*tensors: torch.Tensor) -> None:
+    # dominus_ultra.py:104-116
+    first = tensors[0]
+    if not first.is_cuda:
+        raise ValueError("DominusUltra kernels require CUDA tensors")
+    if first.dtype not in (torch.float16, torch.bfloat16):
+        raise ValueError("attention tensors must use float16 or bfloat16")
+    for tensor in tensors:
+        if tensor.device != first.device:
+            raise ValueError("all attention tensors must be on the same CUDA device")
+        if tensor.dtype != first.dtype:
+            raise ValueError("all attention tensors must have the same dtype")
+        if not tensor.is_contiguous():
+            raise ValueError("attention tensors must be contiguous")
+
+
+def _dtype_code(dtype: torch.dtype) -> int:
+    if dtype == torch.bfloat16:
+        return _lib.DU_DTYPE_BF16
+    if dtype == torch.float16:
+        return _lib.DU_DTYPE_F16
+    if dtype == torch.float32:
+        return _lib.DU_DTYPE_F32
+    raise ValueError(f"unsupported dtype {dtype}")
+
+
+def _aligned(t: torch.Tensor) -> torch.Tensor:
+    """The kernels read through TMA / 128-bit loads, which need 16-byte aligned bases.
+
+    A contiguous view at an odd storage offset is copied into a fresh (aligned) buffer.
+    """
+    return t if t.data_ptr() % 16 == 0 else t.clone()
+
+
+def _stream(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _ptr(t: Optional[torch.Tensor]) -> ctypes.c_void_p:
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def dominus_ultra_prefill(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    cos: torch.Tensor,
+    sin: torch.Tensor,
+    num_kv_heads: Optional[int] = None,
+) -> Tuple[torch.Tensor, torch.Tensor]:
+    """
+    Prefill phase attention with RoPE and optional Grouped Query Attention.
+
+    Computes causal multi-head attention with fused Rotary Position Embeddings on the B200
+    tensor cores (``du_prefill``). Supports Grouped Query Attention (GQA) and Multi-Query
+    Attention (MQA). Reference: ``dominus_ultra.py:416-501``.
+
+    Args:
+        q: Query tensor of shape [batch, num_heads, seq_len, head_dim]
+        k: Key tensor of shape [batch, num_kv_heads, seq_len, head_dim]
+        v: Value tensor of shape [batch, num_kv_heads, seq_len, head_dim]
+        cos: Pre-computed cosine values from precompute_rope_cos_sin
+        sin: Pre-computed sine values from precompute_rope_cos_sin
+        num_kv_heads: Number of KV heads for GQA. If None, uses num_query_heads (MHA)
+
+    Returns:
+        Tuple of:
+            - out: Output tensor of shape [batch, num_heads, seq_len, head_dim]
+            - lse: Log-sum-exp values (natural log, fp32) of shape [batch, num_heads, seq_len]
+    """
+    if q.ndim != 4 or k.ndim != 4 or v.ndim != 4:
+        raise ValueError("q, k, and v must be rank-4 tensors")
+
+    B, Hq, T, D = q.shape
+    _, Hk, _, _ = k.shape
+    KvH = num_kv_heads if num_kv_heads is not None else Hq
+    if B <= 0 or Hq <= 0 or T <= 0:
+        raise ValueError("batch, heads, and sequence length must be positive")
+    if KvH <= 0 or Hq % KvH != 0:
+        raise ValueError("num_query_heads must be divisible by num_kv_heads")
+    if k.shape != (B, KvH, T, D) or v.shape != (B, KvH, T, D):
+        raise ValueError("k and v must have shape [batch, num_kv_heads, seq_len, head_dim]")
+    if Hk != KvH:
+        raise ValueError("k head count does not match num_kv_heads")
+
+    _validate_head_dim(D)
+    _validate_attention_tensors(q, k, v)
+    _validate_rope_tables(cos, sin, T, D, q.device, q.dtype)
+
+    lib = _lib.load()
+    q, k, v, cos, sin = (_aligned(t) for t in (q, k, v, cos, sin))
+    out = torch.empty_like(q)
+    lse = torch.empty((B, Hq, T), dtype=torch.float32, device=q.device)
+    scale = 1.0 / (D**0.5)
+    with torch.cuda.device(q.device):
+        rc = lib.du_prefill(
+            _ptr(q), _ptr(k), _ptr(v), _ptr(cos), _ptr(sin), _ptr(out), _ptr(lse),
+            B, Hq, KvH, T, D, _dtype_code(q.dtype), scale,
+            min(cos.shape[0], sin.shape[0]), _stream(q.device),
+        )
+    _lib.check(rc, "du_prefill")
+    return out, lse
+
+
+def _workspace(B: int, Hq: int, Hkv: int, L: int, D: int, device) -> Tuple[Optional[torch.Tensor], int]:
+    nbytes = int(_lib.load().du_decode_workspace_size(B, Hq, Hkv, L, D))
+    if nbytes == 0:
+        return None, 0
+    return torch.empty(nbytes, dtype=torch.uint8, device=device), nbytes
+
+
+def dominus_ultra_decode(
+    q_new: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    cos: torch.Tensor,
+    sin: torch.Tensor,
+    num_kv_heads: Optional[int] = None,
+) -> torch.Tensor:
+    """
+    Decode phase attention for autoregressive generation with KV cache.
+
+    Computes attention for a single new token (rotated at position ``past_len``) against
+    cached keys (rotated at positions ``0..past_len-1``) with a split-KV streaming kernel
+    (``du_decode``). Reference: ``dominus_ultra.py:504-583``.
+
+    Args:
+        q_new: New query tensor of shape [batch, num_heads, 1, head_dim]
+        k_cache: Cached key tensor of shape [batch, num_kv_heads, past_len, head_dim]
+        v_cache: Cached value tensor of shape [batch, num_kv_heads, past_len, head_dim]
+        cos: Pre-computed cosine values from precompute_rope_cos_sin
+        sin: Pre-computed sine values from precompute_rope_cos_sin
+        num_kv_heads: Number of KV heads for GQA. If None, uses num_query_heads (MHA)
+
+    Returns:
+        Output tensor of shape [batch, num_heads, 1, head_dim]
+    """
+    if q_new.ndim != 4 or k_cache.ndim != 4 or v_cache.ndim != 4:
+        raise ValueError("q_new, k_cache, and v_cache must be rank-4 tensors")
+
+    B, Hq, _, D = q_new.shape
+    _, Hk, past_T, _ = k_cache.shape
+    KvH = num_kv_heads if num_kv_heads is not None else Hq
+    if q_new.shape[2] != 1:
+        raise ValueError("q_new must contain exactly one sequence position")
+    if B <= 0 or Hq <= 0 or past_T <= 0:
+        raise ValueError("batch, heads, and cache length must be positive")
+    if KvH <= 0 or Hq % KvH != 0:
+        raise ValueError("num_query_heads must be divisible by num_kv_heads")
+    if k_cache.shape != (B, KvH, past_T, D) or v_cache.shape != (B, KvH, past_T, D):
+        raise ValueError("k_cache and v_cache must have matching GQA cache shapes")
+    if Hk != KvH:
+        raise ValueError("cache head count does not match num_kv_heads")
+
+    _validate_head_dim(D)
+    _validate_attention_tensors(q_new, k_cache, v_cache)
+    _validate_rope_tables(cos, sin, past_T + 1, D, q_new.device, q_new.dtype)
+
+    lib = _lib.load()
+    q_new, k_cache, v_cache, cos, sin = (_aligned(t) for t in (q_new, k_cache, v_cache, cos, sin))
+    out = torch.empty_like(q_new).squeeze(2)
+    scale = 1.0 / (D**0.5)
+    with torch.cuda.device(q_new.device):
+        ws, nbytes = _workspace(B, Hq, KvH, past_T, D, q_new.device)
+        rc = lib.du_decode(
+            _ptr(q_new), _ptr(k_cache), _ptr(v_cache), _ptr(cos), _ptr(sin), _ptr(out),
+            B, Hq, KvH, past_T, D, _dtype_code(q_new.dtype), scale,
+            min(cos.shape[0], sin.shape[0]), _ptr(ws), nbytes, _stream(q_new.device),
+        )
+    _lib.check(rc, "du_decode")
+    return out.unsqueeze(2)
+
+
+def decode_partial(
+    q_new: torch.Tensor,
+    k_shard: torch.Tensor,
+    v_shard: torch.Tensor,
+    cos: torch.Tensor,
+    sin: torch.Tensor,
+    num_kv_heads: Optional[int],
+    q_pos: int,
+    kv_pos_offset: int,
+    out: Optional[torch.Tensor] = None,
+    lse: Optional[torch.Tensor] = None,
+) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Decode over one shard of the KV sequence (``du_decode_partial``).
+
+    Keys of the shard sit at absolute positions ``kv_pos_offset + j`` and the query at
+    ``q_pos``. Returns fp32 ``(out [B, Hq, D], lse [B, Hq])`` normalised over the shard, for
+    ``merge_partials``. ``out`` / ``lse`` may be preallocated views (e.g. of a packed buffer).
+    """
+    B, Hq, _, D = q_new.shape
+    L = k_shard.shape[2]
+    KvH = num_kv_heads if num_kv_heads is not None else Hq
+    _validate_head_dim(D)
+    _validate_attention_tensors(q_new, k_shard, v_shard)
+    _validate_rope_tables(cos, sin, max(q_pos, kv_pos_offset + L - 1) + 1, D, q_new.device, q_new.dtype)
+    lib = _lib.load()
+    q_new, k_shard, v_shard, cos, sin = (_aligned(t) for t in (q_new, k_shard, v_shard, cos, sin))
+    if out is None:
+        out = torch.empty((B, Hq, D), dtype=torch.float32, device=q_new.device)
+    if lse is None:
+        lse = torch.empty((B, Hq), dtype=torch.float32, device=q_new.device)
+    with torch.cuda.device(q_new.device):
+        ws, nbytes = _workspace(B, Hq, KvH, L, D, q_new.device)
+        rc = lib.du_decode_partial(
+            _ptr(q_new), _ptr(k_shard), _ptr(v_shard), _ptr(cos), _ptr(sin), _ptr(out), _ptr(lse),
+            B, Hq, KvH, L, D, _dtype_code(q_new.dtype), 1.0 / (D**0.5),
+            int(q_pos), int(kv_pos_offset), min(cos.shape[0], sin.shape[0]),
+            _ptr(ws), nbytes, _stream(q_new.device),
+        )
+    _lib.check(rc, "du_decode_partial")
+    return out, lse
+
+
+def merge_partials(
+    o_parts: torch.Tensor,
+    lse_parts: torch.Tensor,
+    out_dtype: torch.dtype,
+    with_lse: bool = False,
+) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """LSE-weighted merge of ``R`` partials (``du_merge_partials``).
+
+    ``o_parts`` is fp32 ``[R, *rows, D]`` and ``lse_parts`` fp32 ``[R, *rows]`` (any strides
+    along R and a contiguous row block). Returns ``out [*rows, D]`` in ``out_dtype`` and, with
+    ``with_lse``, the merged fp32 ``lse [*rows]``.
+    """
+    if o_parts.dtype != torch.float32 or lse_parts.dtype != torch.float32:
+        raise ValueError("partials must be float32")
+    if not o_parts.is_cuda or not lse_parts.is_cuda:
+        raise ValueError("DominusUltra kernels require CUDA tensors")
+    R = o_parts.shape[0]
+    D = o_parts.shape[-1]
+    row_shape: Sequence[int] = tuple(o_parts.shape[1:-1])
+    if tuple(lse_parts.shape) != (R, *row_shape):
+        raise ValueError("lse_parts must have shape [R, *rows] matching o_parts")
+    o2 = o_parts.reshape(R, -1, D)
+    l2 = lse_parts.reshape(R, -1)
+    if o2.stride(2) != 1 or o2.stride(1) != D or l2.stride(1) != 1:
+        raise ValueError("each partial must be a contiguous [rows, D] / [rows] block")
+    rows = o2.shape[1]
+    out = torch.empty((*row_shape, D), dtype=out_dtype, device=o_parts.device)
+    lse = torch.empty(row_shape, dtype=torch.float32, device=o_parts.device) if with_lse else None
+    lib = _lib.load()
+    with torch.cuda.device(o_parts.device):
+        rc = lib.du_merge_partials(
+            _ptr(o2), _ptr(l2), R, rows, D, o2.stride(0), o2.stride(1), l2.stride(0), l2.stride(1),
+            _ptr(out), _dtype_code(out_dtype), _ptr(lse), _stream(o_parts.device),
+        )
+    _lib.check(rc, "du_merge_partials")
+    return out, lse

@@ -1,0 +1,371 @@
+// C ABI of the B200 fused-RoPE attention library (declared in include/dominus_ultra_b200.h).
+//
+// This translation unit holds the host-side launchers: argument validation, TMA tensor-map
+// encoding (cuTensorMapEncodeTiled reached through the runtime's driver entry point, so the
+// library does not link libcuda directly), decode split planning and the kernel dispatch over
+// head_dim x dtype.
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/dominus_ultra_b200.h"
+#include "decode_sm100.cuh"
+#include "prefill_sm100.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(DU_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool valid_head_dim(int D) { return D == 16 || D == 32 || D == 64 || D == 128 || D == 256; }
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    }
+  });
+  return fn;
+}
+
+// 3-D map over a contiguous [rows_outer, T, D] 16-bit tensor: dims {D, T, rows_outer}, box
+// {box_cols, box_rows, 1}, swizzle matching the box row span, zero fill out of bounds.
+int encode_map(CUtensorMap* map, const void* base, int dtype, int D, int T, long long outer,
+               int box_cols, int box_rows, int span_bytes) {
+  auto fn = get_encode_fn();
+  if (fn == nullptr) return fail(DU_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(T),
+                        static_cast<cuuint64_t>(outer)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * 2,
+                           static_cast<cuuint64_t>(T) * static_cast<cuuint64_t>(D) * 2};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  const CUtensorMapSwizzle sw = span_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : span_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                   : CU_TENSOR_MAP_SWIZZLE_32B;
+  const CUtensorMapDataType dt =
+      dtype == DU_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(DU_ERR_CUDA, "cuTensorMapEncodeTiled failed with CUresult " + std::to_string(r));
+  return DU_OK;
+}
+
+int sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+    return 148;
+  return n;
+}
+
+template <int D, bool BF16>
+int launch_prefill_t(const void* q, const void* k, const void* v, const du::PrefillParams& prm,
+                     int B, cudaStream_t st) {
+  using S = du::PrefillShape<D>;
+  const int dtype = BF16 ? DU_DTYPE_BF16 : DU_DTYPE_F16;
+  CUtensorMap tq, tk, tv;
+  int rc;
+  if ((rc = encode_map(&tq, q, dtype, D, prm.T, static_cast<long long>(B) * prm.Hq, S::SPAN / 2,
+                       S::BM, S::SPAN)) != DU_OK)
+    return rc;
+  if ((rc = encode_map(&tk, k, dtype, D, prm.T, static_cast<long long>(B) * prm.Hkv, S::SPAN / 2,
+                       S::BN, S::SPAN)) != DU_OK)
+    return rc;
+  if ((rc = encode_map(&tv, v, dtype, D, prm.T, static_cast<long long>(B) * prm.Hkv, S::SPAN / 2,
+                       S::BN, S::SPAN)) != DU_OK)
+    return rc;
+  auto kern = du::prefill_kernel<D, BF16>;
+  cudaError_t e =
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM_BYTES);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(prefill)");
+  dim3 grid(static_cast<unsigned>(B * prm.Hq), static_cast<unsigned>(prm.n_qtiles));
+  kern<<<grid, S::NTHREADS, S::SMEM_BYTES, st>>>(tq, tk, tv, prm);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
+  return DU_OK;
+}
+
+struct DecodePlan {
+  int GT;
+  int n_gchunk;
+  int n_split;
+  int keys_per_split;
+};
+
+DecodePlan plan_decode(int B, int Hq, int Hkv, int L) {
+  DecodePlan pl{};
+  const int G = Hq / Hkv;
+  pl.GT = (G % 4 == 0) ? 4 : ((G % 2 == 0) ? 2 : 1);
+  pl.n_gchunk = G / pl.GT;
+  const long long units = static_cast<long long>(B) * Hkv * pl.n_gchunk;
+  const long long target = static_cast<long long>(sm_count()) * 4;  // 128-thread CTAs
+  const int min_keys = 128;
+  long long max_split = (L + min_keys - 1) / min_keys;
+  if (max_split > 4096) max_split = 4096;
+  long long ns = (target + units - 1) / units;
+  if (ns < 1) ns = 1;
+  if (ns > max_split) ns = max_split;
+  const long long kps = (L + ns - 1) / ns;
+  pl.keys_per_split = static_cast<int>(kps);
+  pl.n_split = static_cast<int>((L + kps - 1) / kps);
+  return pl;
+}
+
+size_t decode_ws_bytes(const DecodePlan& pl, int B, int Hq, int D) {
+  if (pl.n_split <= 1) return 0;
+  const size_t rows = static_cast<size_t>(B) * Hq;
+  const size_t o = rows * pl.n_split * D * sizeof(float);
+  const size_t l = rows * pl.n_split * sizeof(float);
+  return ((o + 255) / 256) * 256 + l;
+}
+
+template <int D, bool BF16, int GT>
+int launch_decode_split_t(const du::DecodeParams& prm, int B, cudaStream_t st) {
+  dim3 grid(static_cast<unsigned>(prm.n_split),
+            static_cast<unsigned>(B * prm.Hkv * prm.n_gchunk));
+  du::decode_split_kernel<D, BF16, GT><<<grid, 128, 0, st>>>(prm);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "decode launch");
+  return DU_OK;
+}
+
+template <int D, bool BF16>
+int launch_decode_split_g(const du::DecodeParams& prm, int GT, int B, cudaStream_t st) {
+  switch (GT) {
+    case 4: return launch_decode_split_t<D, BF16, 4>(prm, B, st);
+    case 2: return launch_decode_split_t<D, BF16, 2>(prm, B, st);
+    default: return launch_decode_split_t<D, BF16, 1>(prm, B, st);
+  }
+}
+
+template <bool BF16>
+int launch_decode_split_d(const du::DecodeParams& prm, int GT, int D, int B, cudaStream_t st) {
+  switch (D) {
+    case 16: return launch_decode_split_g<16, BF16>(prm, GT, B, st);
+    case 32: return launch_decode_split_g<32, BF16>(prm, GT, B, st);
+    case 64: return launch_decode_split_g<64, BF16>(prm, GT, B, st);
+    case 128: return launch_decode_split_g<128, BF16>(prm, GT, B, st);
+    case 256: return launch_decode_split_g<256, BF16>(prm, GT, B, st);
+    default: return fail(DU_ERR_UNSUPPORTED, "head_dim must be one of 16, 32, 64, 128, 256");
+  }
+}
+
+int launch_merge(const float* o_parts, const float* lse_parts, int R, int rows, int D,
+                 long long o_sr, long long o_srow, long long l_sr, long long l_srow, void* out,
+                 int out_kind, float* lse_out, cudaStream_t st) {
+  const int threads = D >= 256 ? 256 : (D >= 128 ? 128 : 64);
+  du::merge_kernel<<<rows, threads, 0, st>>>(o_parts, lse_parts, R, D, o_sr, o_srow, l_sr, l_srow,
+                                             out, out_kind, lse_out);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "merge launch");
+  return DU_OK;
+}
+
+int check_common(int B, int Hq, int Hkv, int len, int D, int dtype) {
+  if (B <= 0 || Hq <= 0 || len <= 0)
+    return fail(DU_ERR_INVALID, "batch, heads, and sequence length must be positive");
+  if (Hkv <= 0 || Hq % Hkv != 0)
+    return fail(DU_ERR_INVALID, "num_query_heads must be divisible by num_kv_heads");
+  if (!valid_head_dim(D))
+    return fail(DU_ERR_UNSUPPORTED, "head_dim must be a power of two between 16 and 256");
+  if (dtype != DU_DTYPE_F16 && dtype != DU_DTYPE_BF16)
+    return fail(DU_ERR_INVALID, "dtype must be DU_DTYPE_F16 or DU_DTYPE_BF16");
+  return DU_OK;
+}
+
+// Shared body of du_decode and du_decode_partial.
+int decode_impl(const void* q, const void* kc, const void* vc, const void* cos, const void* sin,
+                void* out, float* out_f32, float* lse_f32, int B, int Hq, int Hkv, int L, int D,
+                int dtype, float scale, long long q_pos, long long kv_off, long long rope_positions,
+                void* ws, size_t ws_bytes, cudaStream_t st) {
+  int rc = check_common(B, Hq, Hkv, L, D, dtype);
+  if (rc != DU_OK) return rc;
+  if (!q || !kc || !vc || !cos || !sin || (!out && !out_f32))
+    return fail(DU_ERR_INVALID, "null pointer argument");
+  if (!aligned16(q) || !aligned16(kc) || !aligned16(vc) || !aligned16(cos) || !aligned16(sin))
+    return fail(DU_ERR_INVALID, "q, caches and rope tables must be 16-byte aligned");
+  if (q_pos < 0 || kv_off < 0 || q_pos >= rope_positions || kv_off + L > rope_positions)
+    return fail(DU_ERR_INVALID, "rope tables do not cover the query / key positions");
+  if (!(scale > 0.f)) return fail(DU_ERR_INVALID, "scale must be positive");
+  const DecodePlan pl = plan_decode(B, Hq, Hkv, L);
+  du::DecodeParams prm{};
+  prm.q = q;
+  prm.k = kc;
+  prm.v = vc;
+  prm.cos = cos;
+  prm.sin = sin;
+  prm.Hq = Hq;
+  prm.Hkv = Hkv;
+  prm.L = L;
+  prm.G = Hq / Hkv;
+  prm.n_gchunk = pl.n_gchunk;
+  prm.n_split = pl.n_split;
+  prm.keys_per_split = pl.keys_per_split;
+  prm.q_pos = q_pos;
+  prm.kv_pos_offset = kv_off;
+  prm.scale_log2 = scale * 1.4426950408889634f;
+  const bool bf16 = dtype == DU_DTYPE_BF16;
+  const long long rows = static_cast<long long>(B) * Hq;
+  if (pl.n_split == 1) {
+    if (out != nullptr) {
+      prm.mode = 0;
+      prm.out = out;
+    } else {
+      prm.mode = 1;
+      prm.o_part = out_f32;
+      prm.lse_part = lse_f32;
+    }
+    return bf16 ? launch_decode_split_d<true>(prm, pl.GT, D, B, st)
+                : launch_decode_split_d<false>(prm, pl.GT, D, B, st);
+  }
+  const size_t need = decode_ws_bytes(pl, B, Hq, D);
+  if (ws == nullptr || ws_bytes < need || !aligned16(ws))
+    return fail(DU_ERR_WORKSPACE, "decode workspace of " + std::to_string(need) +
+                                      " bytes (16-byte aligned) is required");
+  float* o_part = static_cast<float*>(ws);
+  const size_t o_bytes = static_cast<size_t>(rows) * pl.n_split * D * sizeof(float);
+  float* l_part = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + ((o_bytes + 255) / 256) * 256);
+  prm.mode = 1;
+  prm.o_part = o_part;
+  prm.lse_part = l_part;
+  rc = bf16 ? launch_decode_split_d<true>(prm, pl.GT, D, B, st)
+            : launch_decode_split_d<false>(prm, pl.GT, D, B, st);
+  if (rc != DU_OK) return rc;
+  if (out != nullptr)
+    return launch_merge(o_part, l_part, pl.n_split, static_cast<int>(rows), D, D,
+                        static_cast<long long>(pl.n_split) * D, 1, pl.n_split, out, dtype, nullptr,
+                        st);
+  return launch_merge(o_part, l_part, pl.n_split, static_cast<int>(rows), D, D,
+                      static_cast<long long>(pl.n_split) * D, 1, pl.n_split, out_f32, DU_DTYPE_F32,
+                      lse_f32, st);
+}
+
+}  // namespace
+
+extern "C" {
+
+int du_version(void) { return 100; }
+
+const char* du_last_error(void) { return g_last_error.c_str(); }
+
+int du_prefill(const void* q, const void* k, const void* v, const void* cos, const void* sin,
+               void* out, float* lse, int B, int Hq, int Hkv, int T, int D, int dtype,
+               float scale, long long rope_positions, void* stream) {
+  g_last_error.clear();
+  int rc = check_common(B, Hq, Hkv, T, D, dtype);
+  if (rc != DU_OK) return rc;
+  if (!q || !k || !v || !cos || !sin || !out || !lse)
+    return fail(DU_ERR_INVALID, "null pointer argument");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(cos) || !aligned16(sin) ||
+      !aligned16(out) || !aligned16(lse))
+    return fail(DU_ERR_INVALID, "all tensors must be 16-byte aligned");
+  if (rope_positions < T) return fail(DU_ERR_INVALID, "rope tables have fewer than T positions");
+  if (!(scale > 0.f)) return fail(DU_ERR_INVALID, "scale must be positive");
+  if ((T + 127) / 128 > 65535) return fail(DU_ERR_UNSUPPORTED, "sequence length too large");
+  du::PrefillParams prm{};
+  prm.cos = cos;
+  prm.sin = sin;
+  prm.out = out;
+  prm.lse = lse;
+  prm.Hq = Hq;
+  prm.Hkv = Hkv;
+  prm.T = T;
+  prm.n_qtiles = (T + 127) / 128;
+  prm.scale_log2 = scale * 1.4426950408889634f;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool bf16 = dtype == DU_DTYPE_BF16;
+  switch (D) {
+    case 16: return bf16 ? launch_prefill_t<16, true>(q, k, v, prm, B, st)
+                         : launch_prefill_t<16, false>(q, k, v, prm, B, st);
+    case 32: return bf16 ? launch_prefill_t<32, true>(q, k, v, prm, B, st)
+                         : launch_prefill_t<32, false>(q, k, v, prm, B, st);
+    case 64: return bf16 ? launch_prefill_t<64, true>(q, k, v, prm, B, st)
+                         : launch_prefill_t<64, false>(q, k, v, prm, B, st);
+    case 128: return bf16 ? launch_prefill_t<128, true>(q, k, v, prm, B, st)
+                          : launch_prefill_t<128, false>(q, k, v, prm, B, st);
+    case 256: return bf16 ? launch_prefill_t<256, true>(q, k, v, prm, B, st)
+                          : launch_prefill_t<256, false>(q, k, v, prm, B, st);
+    default: return fail(DU_ERR_UNSUPPORTED, "head_dim must be one of 16, 32, 64, 128, 256");
+  }
+}
+
+size_t du_decode_workspace_size(int B, int Hq, int Hkv, int L, int D) {
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || L <= 0 || Hq % Hkv != 0 || !valid_head_dim(D)) return 0;
+  return decode_ws_bytes(plan_decode(B, Hq, Hkv, L), B, Hq, D);
+}
+
+int du_decode(const void* q, const void* k_cache, const void* v_cache, const void* cos,
+              const void* sin, void* out, int B, int Hq, int Hkv, int L, int D, int dtype,
+              float scale, long long rope_positions, void* workspace, size_t workspace_bytes,
+              void* stream) {
+  g_last_error.clear();
+  if (out == nullptr) return fail(DU_ERR_INVALID, "null pointer argument");
+  return decode_impl(q, k_cache, v_cache, cos, sin, out, nullptr, nullptr, B, Hq, Hkv, L, D,
+                     dtype, scale, L, 0, rope_positions, workspace, workspace_bytes,
+                     static_cast<cudaStream_t>(stream));
+}
+
+int du_decode_partial(const void* q, const void* k_shard, const void* v_shard, const void* cos,
+                      const void* sin, float* out_f32, float* lse_f32, int B, int Hq, int Hkv,
+                      int L_shard, int D, int dtype, float scale, long long q_pos,
+                      long long kv_pos_offset, long long rope_positions, void* workspace,
+                      size_t workspace_bytes, void* stream) {
+  g_last_error.clear();
+  if (out_f32 == nullptr || lse_f32 == nullptr)
+    return fail(DU_ERR_INVALID, "null pointer argument");
+  return decode_impl(q, k_shard, v_shard, cos, sin, nullptr, out_f32, lse_f32, B, Hq, Hkv,
+                     L_shard, D, dtype, scale, q_pos, kv_pos_offset, rope_positions, workspace,
+                     workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int du_merge_partials(const float* o_parts, const float* lse_parts, int R, int rows, int D,
+                      long long o_stride_r, long long o_stride_row, long long lse_stride_r,
+                      long long lse_stride_row, void* out, int out_dtype, float* lse_out,
+                      void* stream) {
+  g_last_error.clear();
+  if (R <= 0 || rows <= 0 || D <= 0) return fail(DU_ERR_INVALID, "R, rows and D must be positive");
+  if (!o_parts || !lse_parts || !out) return fail(DU_ERR_INVALID, "null pointer argument");
+  if (out_dtype != DU_DTYPE_F16 && out_dtype != DU_DTYPE_BF16 && out_dtype != DU_DTYPE_F32)
+    return fail(DU_ERR_INVALID, "out_dtype must be DU_DTYPE_F16, BF16 or F32");
+  return launch_merge(o_parts, lse_parts, R, rows, D, o_stride_r, o_stride_row, lse_stride_r,
+                      lse_stride_row, out, out_dtype, lse_out, static_cast<cudaStream_t>(stream));
+}
+
+int du_read_status(unsigned int* words4, int reset) {
+  g_last_error.clear();
+  unsigned int h[4] = {0, 0, 0, 0};
+  cudaError_t e = cudaMemcpyFromSymbol(h, g_du_status, sizeof(h));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyFromSymbol(status)");
+  if (words4 != nullptr) std::memcpy(words4, h, sizeof(h));
+  if (reset) {
+    const unsigned int z[4] = {0, 0, 0, 0};
+    e = cudaMemcpyToSymbol(g_du_status, z, sizeof(z));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyToSymbol(status)");
+  }
+  return DU_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,106 @@
+/*
+ * dominus_ultra_b200.h -- C ABI of the B200 (sm_100a) fused-RoPE causal attention library.
+ *
+ * Plain pointers, sizes and a CUDA stream handle; no framework types. All entry points are
+ * asynchronous on `stream` (a cudaStream_t passed as void*), never synchronise, and return
+ * DU_OK (0) or a DU_ERR_* code; du_last_error() then describes the failure. Arguments are
+ * validated before any launch.
+ *
+ * Layouts (row-major, contiguous, 16-byte aligned base pointers):
+ *   q        [B, Hq, T, D]         k, v      [B, Hkv, T, D]
+ *   cos, sin [positions, D/2]      (half-split RoPE tables, same dtype as q)
+ *   out      [B, Hq, T, D]         lse       [B, Hq, T] fp32, natural log
+ * Query head h reads KV head h / (Hq / Hkv). D is one of 16, 32, 64, 128, 256.
+ * dtype: DU_DTYPE_F16 or DU_DTYPE_BF16 for q/k/v/cos/sin/out.
+ */
+#ifndef DOMINUS_ULTRA_B200_H
+#define DOMINUS_ULTRA_B200_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DU_OK 0
+#define DU_ERR_INVALID 1     /* bad argument (shape, alignment, dtype, null pointer) */
+#define DU_ERR_UNSUPPORTED 2 /* valid but not built (e.g. head_dim outside 16..256) */
+#define DU_ERR_CUDA 3        /* a CUDA runtime / driver call failed */
+#define DU_ERR_WORKSPACE 4   /* workspace missing or too small */
+#define DU_ERR_TIMEOUT 5     /* a bounded device-side wait expired (see du_read_status) */
+
+#define DU_DTYPE_F16 0
+#define DU_DTYPE_BF16 1
+#define DU_DTYPE_F32 2
+
+/* Library version, major * 10000 + minor * 100 + patch. */
+int du_version(void);
+
+/* Description of the last error on the calling host thread ("" if none). */
+const char* du_last_error(void);
+
+/*
+ * Causal fused-RoPE prefill. Replaces the launch of `prefill_kernel` in
+ * `dominus_ultra_prefill` (reference dominus_ultra.py:416-501, kernel :119-285).
+ * Rows use positions 0..T-1 of the tables; `rope_positions` is the table length (>= T).
+ * `scale` is the softmax scale (the reference uses 1/sqrt(D), dominus_ultra.py:475).
+ */
+int du_prefill(const void* q, const void* k, const void* v, const void* cos, const void* sin,
+               void* out, float* lse, int B, int Hq, int Hkv, int T, int D, int dtype,
+               float scale, long long rope_positions, void* stream);
+
+/*
+ * Workspace bytes du_decode / du_decode_partial need for these sizes on the current device
+ * (0 when the cache is handled by a single split per row).
+ */
+size_t du_decode_workspace_size(int B, int Hq, int Hkv, int L, int D);
+
+/*
+ * Decode: one new query token per (batch, head) against a KV cache of length L.
+ * Replaces the launch of `decode_kernel` in `dominus_ultra_decode` (reference
+ * dominus_ultra.py:504-583, kernel :288-413): the query rotates at position L, cached key j at
+ * position j, no mask. q [B, Hq, D] (the reference's [B, Hq, 1, D]), caches [B, Hkv, L, D],
+ * out [B, Hq, D]. `rope_positions` must be >= L + 1.
+ */
+int du_decode(const void* q, const void* k_cache, const void* v_cache, const void* cos,
+              const void* sin, void* out, int B, int Hq, int Hkv, int L, int D, int dtype,
+              float scale, long long rope_positions, void* workspace, size_t workspace_bytes,
+              void* stream);
+
+/*
+ * Decode over one shard of a KV sequence (no counterpart in the reference, which has no
+ * multi-GPU path; it generalises decode_kernel, dominus_ultra.py:288-413, by position
+ * offsets). Key j of the shard rotates at kv_pos_offset + j, the query at q_pos. Writes fp32
+ * out_f32 [B, Hq, D] normalised over the shard and lse_f32 [B, Hq] (natural log) for a later
+ * du_merge_partials. Requires q_pos and kv_pos_offset + L_shard - 1 < rope_positions.
+ */
+int du_decode_partial(const void* q, const void* k_shard, const void* v_shard, const void* cos,
+                      const void* sin, float* out_f32, float* lse_f32, int B, int Hq, int Hkv,
+                      int L_shard, int D, int dtype, float scale, long long q_pos,
+                      long long kv_pos_offset, long long rope_positions, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
+/*
+ * LSE-weighted merge of R partial results per row (no counterpart in the reference):
+ * lse = log(sum_r exp(lse_r)), out = sum_r exp(lse_r - lse) * o_r.
+ * Partial r of row i lives at o_parts[r * o_stride_r + i * o_stride_row + d] and
+ * lse_parts[r * lse_stride_r + i * lse_stride_row] (strides in elements).
+ * out [rows, D] in out_dtype (DU_DTYPE_F16 / BF16 / F32); lse_out [rows] may be NULL.
+ */
+int du_merge_partials(const float* o_parts, const float* lse_parts, int R, int rows, int D,
+                      long long o_stride_r, long long o_stride_row, long long lse_stride_r,
+                      long long lse_stride_row, void* out, int out_dtype, float* lse_out,
+                      void* stream);
+
+/*
+ * Read the device status words written when a bounded wait expires:
+ * words[0] = error code (0 ok, DU_ERR_TIMEOUT), [1] wait site, [2..3] block index.
+ * Synchronises the current device. reset != 0 clears them. Returns DU_OK or DU_ERR_CUDA.
+ */
+int du_read_status(unsigned int* words4, int reset);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DOMINUS_ULTRA_B200_H */
