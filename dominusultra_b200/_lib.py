@@ -25,6 +25,8 @@ DU_DTYPE_F16 = 0
 DU_DTYPE_BF16 = 1
 DU_DTYPE_F32 = 2
 
+DU_NOALLOC_SCRATCH_BYTES = 4 << 20  # scratch held by du_decode_noalloc (see the header)
+
 _vp = ctypes.c_void_p
 _i = ctypes.c_int
 _ll = ctypes.c_longlong
@@ -49,6 +51,7 @@ SIGNATURES = {
         _i,
         [_vp, _vp, _i, _i, _i, _ll, _ll, _ll, _ll, _vp, _i, _vp, _vp],
     ),
+    "du_decode_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _ll, _vp]),
     "du_read_status": (_i, [ctypes.POINTER(ctypes.c_uint), _i]),
 }
 

@@ -354,6 +354,73 @@ int du_merge_partials(const float* o_parts, const float* lse_parts, int R, int r
                       lse_stride_row, out, out_dtype, lse_out, static_cast<cudaStream_t>(stream));
 }
 
+}  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// Decode without device allocation (du_decode_noalloc)
+// ---------------------------------------------------------------------------------------------
+// For callers that cannot allocate device memory (a foreign runtime binding this C ABI with no
+// CUDA allocator, or a serving loop that must not call cudaMalloc once running), the split-KV
+// partials live in this fixed array instead of a caller-provided workspace. It is part of the
+// library's device image, so every GPU that loads the library holds these 4 MiB until exit.
+// In host code `g_du_noalloc_scratch` is only a host-side stand-in for the symbol; the device
+// address comes from cudaGetSymbolAddress below, once per device.
+static __device__ __align__(256) unsigned char g_du_noalloc_scratch[DU_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+constexpr int kNoallocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kNoallocMaxDevices] = {};
+
+// Device address of the scratch array on the current device, looked up on first use with that
+// device current (so the first call on a device must not happen inside a stream capture).
+int noalloc_scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kNoallocMaxDevices)
+    return fail(DU_ERR_UNSUPPORTED, "device index beyond the no-allocation scratch table");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_du_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-allocation scratch)");
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return DU_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int du_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, const void* cos,
+                      const void* sin, void* out, int B, int Hq, int Hkv, int L, int D,
+                      int dtype, float scale, long long rope_positions, void* stream) {
+  g_last_error.clear();
+  if (out == nullptr) return fail(DU_ERR_INVALID, "null pointer argument");
+  int rc = check_common(B, Hq, Hkv, L, D, dtype);
+  if (rc != DU_OK) return rc;
+  const size_t need = decode_ws_bytes(plan_decode(B, Hq, Hkv, L), B, Hq, D);
+  if (need > DU_NOALLOC_SCRATCH_BYTES)
+    return fail(DU_ERR_WORKSPACE, "this decode needs " + std::to_string(need) +
+                                      " bytes of split scratch; du_decode_noalloc holds at most " +
+                                      std::to_string(DU_NOALLOC_SCRATCH_BYTES) +
+                                      " bytes (use du_decode with a workspace)");
+  void* scratch = nullptr;
+  if (need > 0) {
+    rc = noalloc_scratch_address(&scratch);
+    if (rc != DU_OK) return rc;
+  }
+  // Nothing in the scratch needs clearing: the split kernel writes every partial the merge
+  // reads. Calls sharing the array must not overlap on the GPU.
+  return decode_impl(q, k_cache, v_cache, cos, sin, out, nullptr, nullptr, B, Hq, Hkv, L, D,
+                     dtype, scale, L, 0, rope_positions, scratch, need,
+                     static_cast<cudaStream_t>(stream));
+}
+
 int du_read_status(unsigned int* words4, int reset) {
   g_last_error.clear();
   unsigned int h[4] = {0, 0, 0, 0};

@@ -93,6 +93,27 @@ int du_merge_partials(const float* o_parts, const float* lse_parts, int R, int r
                       void* stream);
 
 /*
+ * Decode that allocates nothing. No counterpart in the reference: it exists for callers that
+ * cannot allocate device memory themselves -- hosts that bind this C ABI from another runtime
+ * without a CUDA allocator, and serving loops that must not call cudaMalloc once they are
+ * running (it can block on the device and fail under memory pressure).
+ *
+ * Same arguments, semantics and output as du_decode, minus the workspace: the split-KV
+ * partials go to a fixed scratch array of DU_NOALLOC_SCRATCH_BYTES (4 MiB) compiled into this
+ * library, which every GPU that loads the library holds until the process exits. Sizes whose
+ * partials need more than that (see du_decode_workspace_size) are rejected with
+ * DU_ERR_WORKSPACE. The first call on a device looks up that device's address of the array
+ * (cudaGetSymbolAddress, with the device current); make that first call before any stream
+ * capture. All calls on a device share the one array and nothing in it needs clearing (every
+ * partial is written before it is read), so calls that may overlap on the GPU -- on different
+ * streams, or from different host threads -- race; serialise them.
+ */
+#define DU_NOALLOC_SCRATCH_BYTES (4u << 20)
+int du_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, const void* cos,
+                      const void* sin, void* out, int B, int Hq, int Hkv, int L, int D,
+                      int dtype, float scale, long long rope_positions, void* stream);
+
+/*
  * Read the device status words written when a bounded wait expires:
  * words[0] = error code (0 ok, DU_ERR_TIMEOUT), [1] wait site, [2..3] block index.
  * Synchronises the current device. reset != 0 clears them. Returns DU_OK or DU_ERR_CUDA.
