@@ -1,4 +1,5 @@
-// Fused-RoPE decode for sm_100a: split-KV streaming kernel plus an LSE-weighted merge.
+// Fused-RoPE decode for sm_100a: persistent split-KV streaming kernel plus an LSE-weighted
+// merge.
 //
 // One new query token per (batch, query head) attends over a KV cache, rotating the query at
 // position q_pos and key j at position kv_pos_offset + j (reference: decode_kernel,
@@ -7,16 +8,21 @@
 // (the cache holds positions 0..L-1, the new token is at L and does not attend to itself).
 //
 // The kernel is HBM-bound, so it is laid out for streaming:
-//  * a CTA owns one (b, kv head, group chunk) and one contiguous split of the cache, and
-//    serves GT query heads of the GQA group at once, so each KV byte is read once per CTA;
-//  * D/16 lanes share one key row; each lane streams two 16-byte chunks of K and of V
-//    (elements [8c, 8c+8) and [D/2 + 8c, D/2 + 8c + 8)), which are exactly the half-split RoPE
-//    partners, so the rotation needs no shuffles; loads are 128-bit and skip L1;
-//  * scores are reduced across the D/16 lanes with xor-shuffles, the online softmax runs per
-//    lane group in the log2 domain with one rescale per block of U keys, and the groups and
-//    warps are merged at the end;
-//  * with more than one split per row, each split writes an fp32 partial (out normalised over
-//    the split, natural-log LSE) and merge_kernel combines them.
+//  * work items are (unit, split) pairs, where a unit is one (b, kv head, group chunk) serving
+//    GT query heads of the GQA group (so each KV byte is read once) and a split is a
+//    contiguous range of its cache; a persistent grid (resident CTAs only) walks the items;
+//  * a producer warp streams each item's keys in chunks of CK rows: K, V and the matching
+//    cos/sin table rows are contiguous in memory, so each chunk is four cp.async.bulk copies
+//    (no multicast) into a 4-stage shared-memory ring guarded by mbarriers, and it runs ahead
+//    across item boundaries;
+//  * four consumer warps read the ring: D/16 lanes share one key row and each lane takes the
+//    two 16-byte chunks that are half-split RoPE partners (elements [8c, 8c+8) and
+//    [D/2 + 8c, D/2 + 8c + 8)), so the key rotation needs no shuffles; scores are reduced
+//    across the D/16 lanes with xor-shuffles; the online softmax runs per lane group in the
+//    log2 domain, one rescale per chunk;
+//  * at the end of an item the lane groups and warps are merged; with more than one split per
+//    row, each split writes an fp32 partial (out normalised over the split, natural-log LSE)
+//    and merge_kernel combines them.
 #pragma once
 
 #include "du_ptx.cuh"
@@ -39,230 +45,330 @@ struct DecodeParams {
   int n_gchunk;   // G / GT
   int n_split;
   int keys_per_split;
+  int n_items;    // B * Hkv * n_gchunk * n_split
   long long q_pos;
   long long kv_pos_offset;
   float scale_log2;
   int mode;  // 0: final output in dtype (n_split == 1); 1: fp32 partials
 };
 
-template <int D, bool BF16, int GT>
-__global__ void __launch_bounds__(128) decode_split_kernel(const DecodeParams p) {
-  constexpr int LPR = D / 16;      // lanes per key row
-  constexpr int KPW = 32 / LPR;    // keys per warp step
-  constexpr int U = (D >= 128 || GT >= 4) ? 2 : 4;  // steps per block (rows in flight)
-  constexpr int NW = 4;
-  constexpr int HALF = D / 2;
+template <int D, int GT>
+struct DecodeShape {
+  static constexpr int CK = 4096 / D;       // keys per ring stage
+  static constexpr int NSTG = 4;
+  static constexpr int ROWB = 2 * D;        // bytes per K / V row
+  static constexpr int TABB = D;            // bytes per cos / sin row (D/2 16-bit values)
+  static constexpr int OFF_K = 0;
+  static constexpr int OFF_V = CK * ROWB;
+  static constexpr int OFF_C = 2 * CK * ROWB;
+  static constexpr int OFF_S = OFF_C + CK * TABB;
+  static constexpr int STAGE = OFF_S + CK * TABB;  // 24 KB
+  static constexpr int LPR = D / 16;        // lanes per key row
+  static constexpr int KPW = 32 / LPR;      // keys per warp step
+  static constexpr int NW = 4;              // consumer warps
+  static constexpr int STEPS = CK / (NW * KPW);  // steps per warp per chunk
+  static constexpr int OFF_BAR = NSTG * STAGE;  // full[NSTG], empty[NSTG], merge[2], flag
+  static constexpr int OFF_MERGE = OFF_BAR + 8 * (2 * NSTG + 2) + 16;
+  static constexpr int MERGE_BYTES = NW * GT * (D + 2) * 4;
+  static constexpr int SMEM_BYTES = OFF_MERGE + MERGE_BYTES + 128;  // + alignment slack
+  static constexpr int NTHREADS = 160;
+  static_assert(STEPS == 2, "chunk geometry");
+};
 
-  __shared__ float sm_m[NW][GT];
-  __shared__ float sm_l[NW][GT];
-  __shared__ float sm_acc[NW][GT][D];
+template <int D, bool BF16, int GT>
+__global__ void __launch_bounds__(160) decode_kernel(const DecodeParams p) {
+  using S = DecodeShape<D, GT>;
+  constexpr int LPR = S::LPR, KPW = S::KPW, NSTG = S::NSTG, CK = S::CK, HALF = D / 2;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_u32 = smem_u32(smem_raw);
+  const uint32_t sbase = (raw_u32 + 127u) & ~127u;
+  uint8_t* sgen = smem_raw + (sbase - raw_u32);
+  auto FULL = [&](int s) { return sbase + S::OFF_BAR + 8u * static_cast<uint32_t>(s); };
+  auto EMPTY = [&](int s) { return sbase + S::OFF_BAR + 8u * static_cast<uint32_t>(NSTG + s); };
+  auto MERGE = [&](int i) { return sbase + S::OFF_BAR + 8u * static_cast<uint32_t>(2 * NSTG + i); };
+  volatile int* failed = reinterpret_cast<volatile int*>(sgen + S::OFF_BAR + 8 * (2 * NSTG + 2));
+  float* sm_m = reinterpret_cast<float*>(sgen + S::OFF_MERGE);      // [NW][GT]
+  float* sm_l = sm_m + S::NW * GT;                                   // [NW][GT]
+  float* sm_acc = sm_l + S::NW * GT;                                 // [NW][GT][D]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int kg = lane / LPR;
-  const int c = lane % LPR;
-  const int unit = blockIdx.y;
-  const int gch = unit % p.n_gchunk;
-  const int bk = unit / p.n_gchunk;  // b * Hkv + kvh
-  const int b = bk / p.Hkv;
-  const int kvh = bk - b * p.Hkv;
-  const int h0 = kvh * p.G + gch * GT;
-  const int split = blockIdx.x;
-  const int kbeg = split * p.keys_per_split;
-  const int kend = min(p.L, kbeg + p.keys_per_split);
-
-  const uint8_t* cosb = static_cast<const uint8_t*>(p.cos);
-  const uint8_t* sinb = static_cast<const uint8_t*>(p.sin);
-
-  // Rotated, pre-scaled query halves for this lane's 8 element pairs.
-  float q1[GT][8], q2[GT][8];
-  {
-    const size_t trow = static_cast<size_t>(p.q_pos) * HALF * 2;
-    const uint4 cv = ldg_v4(cosb + trow + c * 16);
-    const uint4 sv = ldg_v4(sinb + trow + c * 16);
-    const uint32_t ca[4] = {cv.x, cv.y, cv.z, cv.w};
-    const uint32_t sa[4] = {sv.x, sv.y, sv.z, sv.w};
-#pragma unroll
-    for (int g = 0; g < GT; ++g) {
-      const uint8_t* qp =
-          static_cast<const uint8_t*>(p.q) + (static_cast<size_t>(b) * p.Hq + h0 + g) * D * 2;
-      const uint4 x1 = ldg_v4(qp + c * 16);
-      const uint4 x2 = ldg_v4(qp + HALF * 2 + c * 16);
-      const uint32_t xa[4] = {x1.x, x1.y, x1.z, x1.w};
-      const uint32_t xb[4] = {x2.x, x2.y, x2.z, x2.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 lo = unpack2<BF16>(xa[i]);
-        const float2 hi = unpack2<BF16>(xb[i]);
-        const float2 cc = unpack2<BF16>(ca[i]);
-        const float2 ss = unpack2<BF16>(sa[i]);
-        q1[g][2 * i] = (lo.x * cc.x - hi.x * ss.x) * p.scale_log2;
-        q1[g][2 * i + 1] = (lo.y * cc.y - hi.y * ss.y) * p.scale_log2;
-        q2[g][2 * i] = (hi.x * cc.x + lo.x * ss.x) * p.scale_log2;
-        q2[g][2 * i + 1] = (hi.y * cc.y + lo.y * ss.y) * p.scale_log2;
-      }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NSTG; ++s) {
+      mbar_init(FULL(s), 1);
+      mbar_init(EMPTY(s), S::NW);
     }
-  }
-
-  float m[GT], l[GT], acc[GT][16];
-#pragma unroll
-  for (int g = 0; g < GT; ++g) {
-    m[g] = -1e30f;
-    l[g] = 0.f;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) acc[g][i] = 0.f;
-  }
-
-  const uint8_t* kb_ptr = static_cast<const uint8_t*>(p.k) + static_cast<size_t>(bk) * p.L * D * 2;
-  const uint8_t* vb_ptr = static_cast<const uint8_t*>(p.v) + static_cast<size_t>(bk) * p.L * D * 2;
-
-  for (int kb = kbeg + warp * KPW * U; kb < kend; kb += NW * KPW * U) {
-    uint4 kx1[U], kx2[U], vx1[U], vx2[U], cvv[U], svv[U];
-    bool valid[U];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int key = kb + u * KPW + kg;
-      valid[u] = key < kend;
-      if (valid[u]) {
-        const size_t ro = static_cast<size_t>(key) * D * 2;
-        kx1[u] = ldg_stream_v4(kb_ptr + ro + c * 16);
-        kx2[u] = ldg_stream_v4(kb_ptr + ro + HALF * 2 + c * 16);
-        vx1[u] = ldg_stream_v4(vb_ptr + ro + c * 16);
-        vx2[u] = ldg_stream_v4(vb_ptr + ro + HALF * 2 + c * 16);
-        const size_t trow = static_cast<size_t>(p.kv_pos_offset + key) * HALF * 2;
-        cvv[u] = ldg_v4(cosb + trow + c * 16);
-        svv[u] = ldg_v4(sinb + trow + c * 16);
-      } else {
-        kx1[u] = kx2[u] = vx1[u] = vx2[u] = cvv[u] = svv[u] = make_uint4(0, 0, 0, 0);
-      }
-    }
-    float sc[U][GT];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const uint32_t xa[4] = {kx1[u].x, kx1[u].y, kx1[u].z, kx1[u].w};
-      const uint32_t xb[4] = {kx2[u].x, kx2[u].y, kx2[u].z, kx2[u].w};
-      const uint32_t ca[4] = {cvv[u].x, cvv[u].y, cvv[u].z, cvv[u].w};
-      const uint32_t sa[4] = {svv[u].x, svv[u].y, svv[u].z, svv[u].w};
-      float k1[8], k2[8];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 lo = unpack2<BF16>(xa[i]);
-        const float2 hi = unpack2<BF16>(xb[i]);
-        const float2 cc = unpack2<BF16>(ca[i]);
-        const float2 ss = unpack2<BF16>(sa[i]);
-        k1[2 * i] = lo.x * cc.x - hi.x * ss.x;
-        k1[2 * i + 1] = lo.y * cc.y - hi.y * ss.y;
-        k2[2 * i] = hi.x * cc.x + lo.x * ss.x;
-        k2[2 * i + 1] = hi.y * cc.y + lo.y * ss.y;
-      }
-#pragma unroll
-      for (int g = 0; g < GT; ++g) {
-        float d = 0.f;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) d = fmaf(q1[g][i], k1[i], fmaf(q2[g][i], k2[i], d));
-#pragma unroll
-        for (int o = LPR / 2; o >= 1; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-        sc[u][g] = valid[u] ? d : -INFINITY;
-      }
-    }
-    float vf[U][16];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const uint32_t va[4] = {vx1[u].x, vx1[u].y, vx1[u].z, vx1[u].w};
-      const uint32_t vb[4] = {vx2[u].x, vx2[u].y, vx2[u].z, vx2[u].w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 a = unpack2<BF16>(va[i]);
-        const float2 bb = unpack2<BF16>(vb[i]);
-        vf[u][2 * i] = a.x;
-        vf[u][2 * i + 1] = a.y;
-        vf[u][8 + 2 * i] = bb.x;
-        vf[u][8 + 2 * i + 1] = bb.y;
-      }
-    }
-#pragma unroll
-    for (int g = 0; g < GT; ++g) {
-      float mb = sc[0][g];
-#pragma unroll
-      for (int u = 1; u < U; ++u) mb = fmaxf(mb, sc[u][g]);
-      const float mn = fmaxf(m[g], mb);
-      const float alpha = ex2(m[g] - mn);
-      l[g] *= alpha;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) acc[g][i] *= alpha;
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const float pe = ex2(sc[u][g] - mn);
-        l[g] += pe;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) acc[g][i] = fmaf(pe, vf[u][i], acc[g][i]);
-      }
-      m[g] = mn;
-    }
-  }
-
-  // Merge the KPW key groups of the warp (butterfly over lanes with the same chunk index).
-#pragma unroll
-  for (int o = LPR; o < 32; o <<= 1) {
-#pragma unroll
-    for (int g = 0; g < GT; ++g) {
-      const float mo = __shfl_xor_sync(0xffffffffu, m[g], o);
-      const float lo = __shfl_xor_sync(0xffffffffu, l[g], o);
-      const float mn = fmaxf(m[g], mo);
-      const float wa = ex2(m[g] - mn);
-      const float wb = ex2(mo - mn);
-      l[g] = l[g] * wa + lo * wb;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float ao = __shfl_xor_sync(0xffffffffu, acc[g][i], o);
-        acc[g][i] = acc[g][i] * wa + ao * wb;
-      }
-      m[g] = mn;
-    }
-  }
-  if (kg == 0) {
-#pragma unroll
-    for (int g = 0; g < GT; ++g) {
-      if (c == 0) {
-        sm_m[warp][g] = m[g];
-        sm_l[warp][g] = l[g];
-      }
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        sm_acc[warp][g][8 * c + i] = acc[g][i];
-        sm_acc[warp][g][HALF + 8 * c + i] = acc[g][8 + i];
-      }
-    }
+    mbar_init(MERGE(0), 128);  // the 128 consumer threads, once per work item
+    mbar_init(MERGE(1), 128);
+    *failed = 0;
+    mbar_fence_init();
+    fence_proxy_async_smem();
   }
   __syncthreads();
 
-  for (int idx = threadIdx.x; idx < GT * D; idx += blockDim.x) {
-    const int g = idx / D;
-    const int d = idx - g * D;
-    float M = sm_m[0][g];
-#pragma unroll
-    for (int w = 1; w < NW; ++w) M = fmaxf(M, sm_m[w][g]);
-    float Lsum = 0.f, A = 0.f;
-#pragma unroll
-    for (int w = 0; w < NW; ++w) {
-      const float wt = ex2(sm_m[w][g] - M);
-      Lsum += sm_l[w][g] * wt;
-      A += sm_acc[w][g][d] * wt;
-    }
-    const size_t row = static_cast<size_t>(b) * p.Hq + h0 + g;
-    const float val = (Lsum > 0.f) ? A / Lsum : 0.f;
-    if (p.mode == 0) {
-      if constexpr (BF16) {
-        static_cast<__nv_bfloat16*>(p.out)[row * D + d] = __float2bfloat16_rn(val);
-      } else {
-        static_cast<__half*>(p.out)[row * D + d] = __float2half_rn(val);
+  const uint8_t* kbase = static_cast<const uint8_t*>(p.k);
+  const uint8_t* vbase = static_cast<const uint8_t*>(p.v);
+  const uint8_t* cosb = static_cast<const uint8_t*>(p.cos);
+  const uint8_t* sinb = static_cast<const uint8_t*>(p.sin);
+
+  if (warp == S::NW) {
+    // ------------------------------------------------------------------ bulk-copy producer
+    if (lane == 0) {
+      int g = 0;  // chunk counter across items (ring stage / phase)
+      bool ok = true;
+      for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
+        const int unit = item / p.n_split;
+        const int split = item - unit * p.n_split;
+        const int bk = unit / p.n_gchunk;  // b * Hkv + kvh
+        const int kbeg = split * p.keys_per_split;
+        const int kend = min(p.L, kbeg + p.keys_per_split);
+        for (int c0 = kbeg; c0 < kend; c0 += CK, ++g) {
+          const int s = g % NSTG;
+          if (g >= NSTG && !mbar_wait(EMPTY(s), ((g / NSTG) - 1) & 1, failed, 60)) {
+            ok = false;
+            break;
+          }
+          const int n = min(CK, kend - c0);
+          const size_t row0 = static_cast<size_t>(bk) * p.L + c0;
+          const size_t tab0 = static_cast<size_t>(p.kv_pos_offset + c0);
+          const uint32_t st = sbase + s * S::STAGE;
+          mbar_expect_tx(FULL(s), static_cast<uint32_t>(n * (2 * S::ROWB + 2 * S::TABB)));
+          bulk_load(st + S::OFF_K, kbase + row0 * S::ROWB, n * S::ROWB, FULL(s));
+          bulk_load(st + S::OFF_V, vbase + row0 * S::ROWB, n * S::ROWB, FULL(s));
+          bulk_load(st + S::OFF_C, cosb + tab0 * S::TABB, n * S::TABB, FULL(s));
+          bulk_load(st + S::OFF_S, sinb + tab0 * S::TABB, n * S::TABB, FULL(s));
+        }
       }
-    } else {
-      p.o_part[(row * p.n_split + split) * D + d] = val;
-      if (d == 0)
-        p.lse_part[row * p.n_split + split] =
-            (Lsum > 0.f) ? (M + lg2(Lsum)) * 0.69314718055994531f : -INFINITY;
+      // Drain: the last copies land before the CTA may exit.
+      for (int j = (g > NSTG ? g - NSTG : 0); j < g; ++j) mbar_wait_drain(FULL(j % NSTG), (j / NSTG) & 1, 61);
     }
+    __syncwarp();
+    return;
+  }
+
+  // -------------------------------------------------------------------- consumers (warps 0..3)
+  const int kg = lane / LPR;
+  const int c = lane % LPR;
+  // Lane groups of odd keys read the two partner chunks in the opposite order, so the eight
+  // lanes of a shared-memory phase touch eight distinct 16-byte bank groups when D = 64.
+  const bool swap_order = (kg & 1) != 0;
+  int g = 0;
+  bool ok = true;
+  int it = 0;  // items processed by this CTA (merge-barrier phase)
+  for (int item = blockIdx.x; item < p.n_items; item += gridDim.x, ++it) {
+    const int unit = item / p.n_split;
+    const int split = item - unit * p.n_split;
+    const int gch = unit % p.n_gchunk;
+    const int bk = unit / p.n_gchunk;
+    const int b = bk / p.Hkv;
+    const int kvh = bk - b * p.Hkv;
+    const int h0 = kvh * p.G + gch * GT;
+    const int kbeg = split * p.keys_per_split;
+    const int kend = min(p.L, kbeg + p.keys_per_split);
+
+    // Rotated, pre-scaled query halves for this lane's 8 element pairs.
+    float q1[GT][8], q2[GT][8];
+    {
+      const size_t trow = static_cast<size_t>(p.q_pos) * S::TABB;
+      const uint4 cv = ldg_v4(cosb + trow + c * 16);
+      const uint4 sv = ldg_v4(sinb + trow + c * 16);
+      const uint32_t ca[4] = {cv.x, cv.y, cv.z, cv.w};
+      const uint32_t sa[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+      for (int gg = 0; gg < GT; ++gg) {
+        const uint8_t* qp =
+            static_cast<const uint8_t*>(p.q) + (static_cast<size_t>(b) * p.Hq + h0 + gg) * S::ROWB;
+        const uint4 x1 = ldg_v4(qp + c * 16);
+        const uint4 x2 = ldg_v4(qp + HALF * 2 + c * 16);
+        const uint32_t xa[4] = {x1.x, x1.y, x1.z, x1.w};
+        const uint32_t xb[4] = {x2.x, x2.y, x2.z, x2.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 lo = unpack2<BF16>(xa[i]);
+          const float2 hi = unpack2<BF16>(xb[i]);
+          const float2 cc = unpack2<BF16>(ca[i]);
+          const float2 ss = unpack2<BF16>(sa[i]);
+          q1[gg][2 * i] = (lo.x * cc.x - hi.x * ss.x) * p.scale_log2;
+          q1[gg][2 * i + 1] = (lo.y * cc.y - hi.y * ss.y) * p.scale_log2;
+          q2[gg][2 * i] = (hi.x * cc.x + lo.x * ss.x) * p.scale_log2;
+          q2[gg][2 * i + 1] = (hi.y * cc.y + lo.y * ss.y) * p.scale_log2;
+        }
+      }
+    }
+
+    float m[GT], l[GT], acc[GT][16];
+#pragma unroll
+    for (int gg = 0; gg < GT; ++gg) {
+      m[gg] = -1e30f;
+      l[gg] = 0.f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) acc[gg][i] = 0.f;
+    }
+
+    for (int c0 = kbeg; ok && c0 < kend; c0 += CK, ++g) {
+      const int s = g % NSTG;
+      ok = mbar_wait(FULL(s), (g / NSTG) & 1, failed, 62);
+      if (!__all_sync(0xffffffffu, ok)) {
+        ok = false;
+        break;
+      }
+      const int n = min(CK, kend - c0);
+      const uint32_t st = sbase + s * S::STAGE;
+      float sc[S::STEPS][GT];
+      float vf[S::STEPS][16];
+#pragma unroll
+      for (int u = 0; u < S::STEPS; ++u) {
+        const int key = warp * (CK / S::NW) + u * KPW + kg;  // row within the chunk
+        const bool valid = key < n;
+        uint4 kx1 = make_uint4(0, 0, 0, 0), kx2 = kx1, vx1 = kx1, vx2 = kx1, cv = kx1, sv = kx1;
+        if (valid) {
+          const uint32_t kr = st + S::OFF_K + key * S::ROWB;
+          const uint32_t vr = st + S::OFF_V + key * S::ROWB;
+          const int ca = swap_order ? c + LPR : c;
+          const int cb = swap_order ? c : c + LPR;
+          const uint4 ka = ld_shared_v4(kr + ca * 16);
+          const uint4 kb = ld_shared_v4(kr + cb * 16);
+          const uint4 va = ld_shared_v4(vr + ca * 16);
+          const uint4 vb = ld_shared_v4(vr + cb * 16);
+          kx1 = swap_order ? kb : ka;
+          kx2 = swap_order ? ka : kb;
+          vx1 = swap_order ? vb : va;
+          vx2 = swap_order ? va : vb;
+          cv = ld_shared_v4(st + S::OFF_C + key * S::TABB + c * 16);
+          sv = ld_shared_v4(st + S::OFF_S + key * S::TABB + c * 16);
+        }
+        const uint32_t xa[4] = {kx1.x, kx1.y, kx1.z, kx1.w};
+        const uint32_t xb[4] = {kx2.x, kx2.y, kx2.z, kx2.w};
+        const uint32_t cca[4] = {cv.x, cv.y, cv.z, cv.w};
+        const uint32_t ssa[4] = {sv.x, sv.y, sv.z, sv.w};
+        float k1[8], k2[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 lo = unpack2<BF16>(xa[i]);
+          const float2 hi = unpack2<BF16>(xb[i]);
+          const float2 cc = unpack2<BF16>(cca[i]);
+          const float2 ss = unpack2<BF16>(ssa[i]);
+          k1[2 * i] = lo.x * cc.x - hi.x * ss.x;
+          k1[2 * i + 1] = lo.y * cc.y - hi.y * ss.y;
+          k2[2 * i] = hi.x * cc.x + lo.x * ss.x;
+          k2[2 * i + 1] = hi.y * cc.y + lo.y * ss.y;
+        }
+#pragma unroll
+        for (int gg = 0; gg < GT; ++gg) {
+          float d = 0.f;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) d = fmaf(q1[gg][i], k1[i], fmaf(q2[gg][i], k2[i], d));
+#pragma unroll
+          for (int o = LPR / 2; o >= 1; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+          sc[u][gg] = valid ? d : -INFINITY;
+        }
+        const uint32_t va4[4] = {vx1.x, vx1.y, vx1.z, vx1.w};
+        const uint32_t vb4[4] = {vx2.x, vx2.y, vx2.z, vx2.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 a = unpack2<BF16>(va4[i]);
+          const float2 bb = unpack2<BF16>(vb4[i]);
+          vf[u][2 * i] = a.x;
+          vf[u][2 * i + 1] = a.y;
+          vf[u][8 + 2 * i] = bb.x;
+          vf[u][8 + 2 * i + 1] = bb.y;
+        }
+      }
+      // The stage's shared memory has been read into registers: release it to the producer.
+      __syncwarp();
+      if (lane == 0) mbar_arrive(EMPTY(s));
+#pragma unroll
+      for (int gg = 0; gg < GT; ++gg) {
+        float mb = sc[0][gg];
+#pragma unroll
+        for (int u = 1; u < S::STEPS; ++u) mb = fmaxf(mb, sc[u][gg]);
+        const float mn = fmaxf(m[gg], mb);
+        const float alpha = ex2(m[gg] - mn);
+        l[gg] *= alpha;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[gg][i] *= alpha;
+#pragma unroll
+        for (int u = 0; u < S::STEPS; ++u) {
+          const float pe = ex2(sc[u][gg] - mn);
+          l[gg] += pe;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) acc[gg][i] = fmaf(pe, vf[u][i], acc[gg][i]);
+        }
+        m[gg] = mn;
+      }
+    }
+    if (!ok) break;
+
+    // Merge the KPW key groups of the warp (butterfly over lanes with the same chunk index).
+#pragma unroll
+    for (int o = LPR; o < 32; o <<= 1) {
+#pragma unroll
+      for (int gg = 0; gg < GT; ++gg) {
+        const float mo = __shfl_xor_sync(0xffffffffu, m[gg], o);
+        const float lo = __shfl_xor_sync(0xffffffffu, l[gg], o);
+        const float mn = fmaxf(m[gg], mo);
+        const float wa = ex2(m[gg] - mn);
+        const float wb = ex2(mo - mn);
+        l[gg] = l[gg] * wa + lo * wb;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float ao = __shfl_xor_sync(0xffffffffu, acc[gg][i], o);
+          acc[gg][i] = acc[gg][i] * wa + ao * wb;
+        }
+        m[gg] = mn;
+      }
+    }
+    if (kg == 0) {
+#pragma unroll
+      for (int gg = 0; gg < GT; ++gg) {
+        if (c == 0) {
+          sm_m[warp * GT + gg] = m[gg];
+          sm_l[warp * GT + gg] = l[gg];
+        }
+        float* a = sm_acc + (warp * GT + gg) * D;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          a[8 * c + i] = acc[gg][i];
+          a[HALF + 8 * c + i] = acc[gg][8 + i];
+        }
+      }
+    }
+    // Bounded barrier of the four consumer warps (the producer warp keeps streaming).
+    mbar_arrive(MERGE(0));
+    ok = mbar_wait(MERGE(0), it & 1, failed, 63);
+    if (!__all_sync(0xffffffffu, ok)) break;
+    for (int idx = threadIdx.x; idx < GT * D; idx += 128) {
+      const int gg = idx / D;
+      const int d = idx - gg * D;
+      float M = sm_m[gg];
+#pragma unroll
+      for (int w = 1; w < S::NW; ++w) M = fmaxf(M, sm_m[w * GT + gg]);
+      float Lsum = 0.f, A = 0.f;
+#pragma unroll
+      for (int w = 0; w < S::NW; ++w) {
+        const float wt = ex2(sm_m[w * GT + gg] - M);
+        Lsum += sm_l[w * GT + gg] * wt;
+        A += sm_acc[(w * GT + gg) * D + d] * wt;
+      }
+      const size_t row = static_cast<size_t>(b) * p.Hq + h0 + gg;
+      const float val = (Lsum > 0.f) ? A / Lsum : 0.f;
+      if (p.mode == 0) {
+        if constexpr (BF16) {
+          static_cast<__nv_bfloat16*>(p.out)[row * D + d] = __float2bfloat16_rn(val);
+        } else {
+          static_cast<__half*>(p.out)[row * D + d] = __float2half_rn(val);
+        }
+      } else {
+        p.o_part[(row * p.n_split + split) * D + d] = val;
+        if (d == 0)
+          p.lse_part[row * p.n_split + split] =
+              (Lsum > 0.f) ? (M + lg2(Lsum)) * 0.69314718055994531f : -INFINITY;
+      }
+    }
+    mbar_arrive(MERGE(1));  // merge area free for the next item
+    ok = mbar_wait(MERGE(1), it & 1, failed, 64);
+    if (!__all_sync(0xffffffffu, ok)) break;
   }
 }
 
@@ -279,13 +385,13 @@ __global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ o_
   for (int r = 0; r < R; ++r) M = fmaxf(M, lse_parts[r * l_sr + row * l_srow]);
   float W = 0.f;
   if (M != -INFINITY) {
-    for (int r = 0; r < R; ++r) W += __expf(lse_parts[r * l_sr + row * l_srow] - M);
+    for (int r = 0; r < R; ++r) W += expf(lse_parts[r * l_sr + row * l_srow] - M);
   }
   for (int d = threadIdx.x; d < D; d += blockDim.x) {
     float A = 0.f;
     if (M != -INFINITY) {
       for (int r = 0; r < R; ++r) {
-        const float wt = __expf(lse_parts[r * l_sr + row * l_srow] - M);
+        const float wt = expf(lse_parts[r * l_sr + row * l_srow] - M);
         A = fmaf(wt, o_parts[r * o_sr + row * o_srow + d], A);
       }
       A /= W;

@@ -9,11 +9,14 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <set>
+#include <utility>
 #include <string>
 
 #include "../../include/dominus_ultra_b200.h"
 #include "decode_sm100.cuh"
 #include "prefill_sm100.cuh"
+#include "prefill_pair_sm100.cuh"
 
 namespace {
 
@@ -72,6 +75,25 @@ int encode_map(CUtensorMap* map, const void* base, int dtype, int D, int T, long
   return DU_OK;
 }
 
+// 2-D map over a [rows, cols] 16-bit table (no swizzle): box {cols, box_rows}.
+int encode_map_2d(CUtensorMap* map, const void* base, int dtype, int cols, long long rows,
+                  int box_rows) {
+  auto fn = get_encode_fn();
+  if (fn == nullptr) return fail(DU_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapDataType dt =
+      dtype == DU_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(DU_ERR_CUDA, "cuTensorMapEncodeTiled (table) failed with CUresult " + std::to_string(r));
+  return DU_OK;
+}
+
 int sm_count() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 148;
@@ -81,28 +103,69 @@ int sm_count() {
   return n;
 }
 
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device). The cache is
+// keyed by the kernel's address: every instantiation shares one function-pointer type.
+template <typename Kern>
+cudaError_t ensure_smem_attr(Kern kern, int bytes) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const auto key = std::make_pair(reinterpret_cast<const void*>(kern), dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count(key)) return cudaSuccess;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.insert(key);
+  return e;
+}
+
 template <int D, bool BF16>
-int launch_prefill_t(const void* q, const void* k, const void* v, const du::PrefillParams& prm,
-                     int B, cudaStream_t st) {
-  using S = du::PrefillShape<D>;
+int launch_prefill_t(const void* q, const void* k, const void* v, du::PrefillParams prm, int B,
+                     long long rope_positions, cudaStream_t st) {
   const int dtype = BF16 ? DU_DTYPE_BF16 : DU_DTYPE_F16;
   CUtensorMap tq, tk, tv;
   int rc;
-  if ((rc = encode_map(&tq, q, dtype, D, prm.T, static_cast<long long>(B) * prm.Hq, S::SPAN / 2,
-                       S::BM, S::SPAN)) != DU_OK)
-    return rc;
-  if ((rc = encode_map(&tk, k, dtype, D, prm.T, static_cast<long long>(B) * prm.Hkv, S::SPAN / 2,
-                       S::BN, S::SPAN)) != DU_OK)
-    return rc;
-  if ((rc = encode_map(&tv, v, dtype, D, prm.T, static_cast<long long>(B) * prm.Hkv, S::SPAN / 2,
-                       S::BN, S::SPAN)) != DU_OK)
-    return rc;
-  auto kern = du::prefill_kernel<D, BF16>;
-  cudaError_t e =
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM_BYTES);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(prefill)");
-  dim3 grid(static_cast<unsigned>(B * prm.Hq), static_cast<unsigned>(prm.n_qtiles));
-  kern<<<grid, S::NTHREADS, S::SMEM_BYTES, st>>>(tq, tk, tv, prm);
+  cudaError_t e;
+  if constexpr (D <= 128) {
+    // Two query tiles per CTA.
+    using S = du::PairShape<D>;
+    CUtensorMap tc, ts;
+    if ((rc = encode_map(&tq, q, dtype, D, prm.T, static_cast<long long>(B) * prm.Hq, S::SPAN / 2,
+                         S::BM, S::SPAN)) != DU_OK)
+      return rc;
+    if ((rc = encode_map(&tk, k, dtype, D, prm.T, static_cast<long long>(B) * prm.Hkv,
+                         S::SPAN / 2, S::BN, S::SPAN)) != DU_OK)
+      return rc;
+    if ((rc = encode_map(&tv, v, dtype, D, prm.T, static_cast<long long>(B) * prm.Hkv,
+                         S::SPAN / 2, S::BN, S::SPAN)) != DU_OK)
+      return rc;
+    if ((rc = encode_map_2d(&tc, prm.cos, dtype, D / 2, rope_positions, S::BN)) != DU_OK) return rc;
+    if ((rc = encode_map_2d(&ts, prm.sin, dtype, D / 2, rope_positions, S::BN)) != DU_OK) return rc;
+    prm.n_qtiles = (prm.T + 2 * S::BM - 1) / (2 * S::BM);  // query-tile pairs
+    auto kern = du::prefill_pair_kernel<D, BF16>;
+    e = ensure_smem_attr(kern, S::SMEM_BYTES);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(prefill)");
+    dim3 grid(static_cast<unsigned>(B * prm.Hq), static_cast<unsigned>(prm.n_qtiles));
+    kern<<<grid, S::NTHREADS, S::SMEM_BYTES, st>>>(tq, tk, tv, tc, ts, prm);
+  } else {
+    using S = du::PrefillShape<D>;
+    if ((rc = encode_map(&tq, q, dtype, D, prm.T, static_cast<long long>(B) * prm.Hq, S::SPAN / 2,
+                         S::BM, S::SPAN)) != DU_OK)
+      return rc;
+    if ((rc = encode_map(&tk, k, dtype, D, prm.T, static_cast<long long>(B) * prm.Hkv,
+                         S::SPAN / 2, S::BN, S::SPAN)) != DU_OK)
+      return rc;
+    if ((rc = encode_map(&tv, v, dtype, D, prm.T, static_cast<long long>(B) * prm.Hkv,
+                         S::SPAN / 2, S::BN, S::SPAN)) != DU_OK)
+      return rc;
+    prm.n_qtiles = (prm.T + S::BM - 1) / S::BM;
+    auto kern = du::prefill_kernel<D, BF16>;
+    e = ensure_smem_attr(kern, S::SMEM_BYTES);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(prefill)");
+    dim3 grid(static_cast<unsigned>(B * prm.Hq), static_cast<unsigned>(prm.n_qtiles));
+    kern<<<grid, S::NTHREADS, S::SMEM_BYTES, st>>>(tq, tk, tv, prm);
+  }
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
   return DU_OK;
@@ -115,20 +178,27 @@ struct DecodePlan {
   int keys_per_split;
 };
 
-DecodePlan plan_decode(int B, int Hq, int Hkv, int L) {
+// Work items are (unit, split); a persistent grid of resident CTAs walks them. Units are
+// (b, kv head, group chunk of GT query heads). When units alone cannot fill about four items
+// per resident CTA slot (two CTAs per SM by shared memory), each cache is split into
+// contiguous ranges whose length is a multiple of the kernel's chunk.
+DecodePlan plan_decode(int B, int Hq, int Hkv, int L, int D) {
   DecodePlan pl{};
   const int G = Hq / Hkv;
   pl.GT = (G % 4 == 0) ? 4 : ((G % 2 == 0) ? 2 : 1);
   pl.n_gchunk = G / pl.GT;
   const long long units = static_cast<long long>(B) * Hkv * pl.n_gchunk;
-  const long long target = static_cast<long long>(sm_count()) * 4;  // 128-thread CTAs
-  const int min_keys = 128;
-  long long max_split = (L + min_keys - 1) / min_keys;
-  if (max_split > 4096) max_split = 4096;
-  long long ns = (target + units - 1) / units;
-  if (ns < 1) ns = 1;
-  if (ns > max_split) ns = max_split;
-  const long long kps = (L + ns - 1) / ns;
+  const long long slots = static_cast<long long>(sm_count()) * 2;
+  const int chunk = 4096 / D;  // DecodeShape<D>::CK
+  long long ns = 1;
+  if (units < slots) {
+    ns = (4 * slots + units - 1) / units;
+    const long long max_split = (L + 2 * chunk - 1) / (2 * chunk);  // >= 2 chunks per split
+    if (ns > max_split) ns = max_split;
+    if (ns < 1) ns = 1;
+  }
+  long long kps = (L + ns - 1) / ns;
+  kps = ((kps + chunk - 1) / chunk) * chunk;
   pl.keys_per_split = static_cast<int>(kps);
   pl.n_split = static_cast<int>((L + kps - 1) / kps);
   return pl;
@@ -144,10 +214,27 @@ size_t decode_ws_bytes(const DecodePlan& pl, int B, int Hq, int D) {
 
 template <int D, bool BF16, int GT>
 int launch_decode_split_t(const du::DecodeParams& prm, int B, cudaStream_t st) {
-  dim3 grid(static_cast<unsigned>(prm.n_split),
-            static_cast<unsigned>(B * prm.Hkv * prm.n_gchunk));
-  du::decode_split_kernel<D, BF16, GT><<<grid, 128, 0, st>>>(prm);
-  cudaError_t e = cudaGetLastError();
+  (void)B;
+  using S = du::DecodeShape<D, GT>;
+  auto kern = du::decode_kernel<D, BF16, GT>;
+  cudaError_t e = ensure_smem_attr(kern, S::SMEM_BYTES);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(decode)");
+  // Resident CTAs per SM, once per instantiation and device (this function is a distinct
+  // template instance per kernel, so the static table is per kernel).
+  static int per_sm_cache[64] = {};
+  int dev = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  int per_sm = (dev >= 0 && dev < 64) ? per_sm_cache[dev] : 0;
+  if (per_sm == 0) {
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, S::NTHREADS, S::SMEM_BYTES);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+    if (per_sm < 1) per_sm = 1;
+    if (dev >= 0 && dev < 64) per_sm_cache[dev] = per_sm;
+  }
+  long long grid = static_cast<long long>(sm_count()) * per_sm;
+  if (grid > prm.n_items) grid = prm.n_items;
+  kern<<<static_cast<unsigned>(grid), S::NTHREADS, S::SMEM_BYTES, st>>>(prm);
+  e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "decode launch");
   return DU_OK;
 }
@@ -210,7 +297,7 @@ int decode_impl(const void* q, const void* kc, const void* vc, const void* cos, 
   if (q_pos < 0 || kv_off < 0 || q_pos >= rope_positions || kv_off + L > rope_positions)
     return fail(DU_ERR_INVALID, "rope tables do not cover the query / key positions");
   if (!(scale > 0.f)) return fail(DU_ERR_INVALID, "scale must be positive");
-  const DecodePlan pl = plan_decode(B, Hq, Hkv, L);
+  const DecodePlan pl = plan_decode(B, Hq, Hkv, L, D);
   du::DecodeParams prm{};
   prm.q = q;
   prm.k = kc;
@@ -224,6 +311,7 @@ int decode_impl(const void* q, const void* kc, const void* vc, const void* cos, 
   prm.n_gchunk = pl.n_gchunk;
   prm.n_split = pl.n_split;
   prm.keys_per_split = pl.keys_per_split;
+  prm.n_items = B * Hkv * pl.n_gchunk * pl.n_split;
   prm.q_pos = q_pos;
   prm.kv_pos_offset = kv_off;
   prm.scale_log2 = scale * 1.4426950408889634f;
@@ -298,23 +386,23 @@ int du_prefill(const void* q, const void* k, const void* v, const void* cos, con
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool bf16 = dtype == DU_DTYPE_BF16;
   switch (D) {
-    case 16: return bf16 ? launch_prefill_t<16, true>(q, k, v, prm, B, st)
-                         : launch_prefill_t<16, false>(q, k, v, prm, B, st);
-    case 32: return bf16 ? launch_prefill_t<32, true>(q, k, v, prm, B, st)
-                         : launch_prefill_t<32, false>(q, k, v, prm, B, st);
-    case 64: return bf16 ? launch_prefill_t<64, true>(q, k, v, prm, B, st)
-                         : launch_prefill_t<64, false>(q, k, v, prm, B, st);
-    case 128: return bf16 ? launch_prefill_t<128, true>(q, k, v, prm, B, st)
-                          : launch_prefill_t<128, false>(q, k, v, prm, B, st);
-    case 256: return bf16 ? launch_prefill_t<256, true>(q, k, v, prm, B, st)
-                          : launch_prefill_t<256, false>(q, k, v, prm, B, st);
+    case 16: return bf16 ? launch_prefill_t<16, true>(q, k, v, prm, B, rope_positions, st)
+                         : launch_prefill_t<16, false>(q, k, v, prm, B, rope_positions, st);
+    case 32: return bf16 ? launch_prefill_t<32, true>(q, k, v, prm, B, rope_positions, st)
+                         : launch_prefill_t<32, false>(q, k, v, prm, B, rope_positions, st);
+    case 64: return bf16 ? launch_prefill_t<64, true>(q, k, v, prm, B, rope_positions, st)
+                         : launch_prefill_t<64, false>(q, k, v, prm, B, rope_positions, st);
+    case 128: return bf16 ? launch_prefill_t<128, true>(q, k, v, prm, B, rope_positions, st)
+                          : launch_prefill_t<128, false>(q, k, v, prm, B, rope_positions, st);
+    case 256: return bf16 ? launch_prefill_t<256, true>(q, k, v, prm, B, rope_positions, st)
+                          : launch_prefill_t<256, false>(q, k, v, prm, B, rope_positions, st);
     default: return fail(DU_ERR_UNSUPPORTED, "head_dim must be one of 16, 32, 64, 128, 256");
   }
 }
 
 size_t du_decode_workspace_size(int B, int Hq, int Hkv, int L, int D) {
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || L <= 0 || Hq % Hkv != 0 || !valid_head_dim(D)) return 0;
-  return decode_ws_bytes(plan_decode(B, Hq, Hkv, L), B, Hq, D);
+  return decode_ws_bytes(plan_decode(B, Hq, Hkv, L, D), B, Hq, D);
 }
 
 int du_decode(const void* q, const void* k_cache, const void* v_cache, const void* cos,
@@ -403,7 +491,7 @@ int du_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, c
   if (out == nullptr) return fail(DU_ERR_INVALID, "null pointer argument");
   int rc = check_common(B, Hq, Hkv, L, D, dtype);
   if (rc != DU_OK) return rc;
-  const size_t need = decode_ws_bytes(plan_decode(B, Hq, Hkv, L), B, Hq, D);
+  const size_t need = decode_ws_bytes(plan_decode(B, Hq, Hkv, L, D), B, Hq, D);
   if (need > DU_NOALLOC_SCRATCH_BYTES)
     return fail(DU_ERR_WORKSPACE, "this decode needs " + std::to_string(need) +
                                       " bytes of split scratch; du_decode_noalloc holds at most " +
@@ -420,6 +508,14 @@ int du_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, c
                      dtype, scale, L, 0, rope_positions, scratch, need,
                      static_cast<cudaStream_t>(stream));
 }
+
+#ifdef DU_TRACE
+// Debug builds only: copy the prefill event trace (16 x 64 timestamps) to the host.
+int du_trace_read(long long* out) {
+  cudaError_t e = cudaMemcpyFromSymbol(out, g_du_trace, sizeof(long long) * 16 * 64);
+  return e == cudaSuccess ? DU_OK : DU_ERR_CUDA;
+}
+#endif
 
 int du_read_status(unsigned int* words4, int reset) {
   g_last_error.clear();

@@ -74,6 +74,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Parity wait that lets the hardware suspend the thread for up to `hint_ns` while the phase is
+// incomplete (the thread resumes when the phase completes), so waiting warps leave their issue
+// slots to the warps doing the work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded parity wait. `failed` is a per-CTA shared flag: once any thread of the CTA has timed
 // out, every later slow wait gives up at once, so the whole CTA drains quickly.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* failed,
@@ -82,7 +97,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   const uint64_t t0 = globaltimer();
   uint32_t n = 0;
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
     if ((++n & 63u) == 0u) {
       if (*failed) return false;
       if (globaltimer() - t0 > DU_WAIT_TIMEOUT_NS) {
@@ -124,12 +139,30 @@ __device__ __forceinline__ void tma_prefetch_desc(const void* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
 
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* map, uint32_t bar, int c0,
+                                            int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(map), "r"(bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* map, uint32_t bar, int c0,
                                             int c1, int c2) {
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
       "l"(map), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+// Contiguous global -> shared copy on the async proxy, completing `bytes` on `bar`
+// (both addresses 16-byte aligned, size a multiple of 16). No multicast.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar)
       : "memory");
 }
 
@@ -170,6 +203,18 @@ __device__ __forceinline__ void umma_f16_ss(uint32_t d_tmem, uint64_t a_desc, ui
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem], kind::f16: A (M x 16, 16-bit) read from tensor memory,
+// two elements per 32-bit column, one row per lane.
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive once on `bar` when every tcgen05 async operation issued so far by this thread is done.
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile(
@@ -205,12 +250,31 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
       : "memory");
 }
 
+__device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Per-warpgroup register budget change (all warps of the warpgroup execute the same one).
+template <int N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -270,6 +334,55 @@ __device__ __forceinline__ float lg2(float x) {
   float y;
   asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Packed fp32 pairs (Blackwell f32x2 arithmetic: one instruction for two lanes of math).
+__device__ __forceinline__ uint64_t f2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float2 f2_split(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x for two values on the FMA pipe (relieves the MUFU unit, which runs 16 exponentials per
+// clock per SM). x is clamped to >= -125; x = j + f with j = round(x) (added in fp32 to
+// 1.5 * 2^23, which leaves j in the low mantissa bits) and f in [-1/2, 1/2]; 2^f by a cubic,
+// 2^j by adding j to the exponent field. The cubic's coefficients are a minimax fit of 2^f on
+// [-1/2, 1/2] (Lawson's iteratively reweighted least squares on relative error, done for this
+// kernel); evaluated in fp32 its relative error is below 7.5e-5, far under the 16-bit rounding
+// P receives afterwards.
+__device__ __forceinline__ float2 ex2_poly2(float x0, float x1) {
+  constexpr float C0 = 0x1.fff692p-1f, C1 = 0x1.62f31ap-1f, C2 = 0x1.f0de1ap-3f, C3 = 0x1.c3f76p-5f;
+  const uint64_t X = f2(fmaxf(x0, -125.0f), fmaxf(x1, -125.0f));
+  const uint64_t T = f2_add(X, f2(12582912.0f, 12582912.0f));
+  const uint64_t J = f2_add(T, f2(-12582912.0f, -12582912.0f));
+  const uint64_t F = f2_fma(J, f2(-1.0f, -1.0f), X);
+  uint64_t P = f2_fma(f2(C3, C3), F, f2(C2, C2));
+  P = f2_fma(P, F, f2(C1, C1));
+  P = f2_fma(P, F, f2(C0, C0));
+  const float2 t = f2_split(T);
+  const float2 pp = f2_split(P);
+  return make_float2(__uint_as_float(__float_as_uint(pp.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(pp.y) + (__float_as_uint(t.y) << 23)));
 }
 
 template <bool BF16>

@@ -26,6 +26,19 @@
 
 #include "du_ptx.cuh"
 
+#ifdef DU_TRACE
+// Debug-only event timestamps (SM clock) of the CTA at blockIdx (0, 0): [event][tile].
+__device__ long long g_du_trace[16 * 64];
+#define DU_TRACE_EV(ev, j)                                                            \
+  do {                                                                               \
+    if (blockIdx.x == 0 && blockIdx.y == 0 && (j) < 64) g_du_trace[(ev) * 64 + (j)] = clock64(); \
+  } while (0)
+#else
+#define DU_TRACE_EV(ev, j) \
+  do {                     \
+  } while (0)
+#endif
+
 namespace du {
 
 struct PrefillParams {
@@ -70,33 +83,45 @@ struct PrefillShape {
   static_assert(Q_BYTES % 1024 == 0 && KV_BYTES % 1024 == 0 && P_BYTES % 1024 == 0, "align");
 };
 
-// Rotate `npairs` chunk pairs of one row of a K-major swizzled tile in place: chunk c holds
-// elements [8c, 8c+8) of the first half, chunk c + D/16 the matching elements of the second
-// half. Input dtype -> fp32 rotation -> fp16 written back (the UMMA operand type).
-template <int D, bool BF16, int SPAN>
+// Load the cos/sin chunks a thread needs for one row: chunk c = c0 + i * cstep holds table
+// entries [8c, 8c + 8) of the half-width row. All loads are issued together (they are L2 hits
+// shared by every CTA) so their latency is paid once per tile, ahead of the tile's TMA wait.
+template <int NP>
+__device__ __forceinline__ void load_rope_row(uint4 (&cv)[NP], uint4 (&sv)[NP], const uint8_t* cos_row,
+                                              const uint8_t* sin_row, int c0, int cstep) {
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    cv[i] = ldg_v4(cos_row + (c0 + i * cstep) * 16);
+    sv[i] = ldg_v4(sin_row + (c0 + i * cstep) * 16);
+  }
+}
+
+// Rotate NP chunk pairs of one row of a K-major swizzled tile in place: chunk c holds elements
+// [8c, 8c+8) of the first half, chunk c + D/16 the matching elements of the second half.
+// Input dtype -> fp32 rotation -> fp16 written back (the UMMA operand type).
+template <int D, bool BF16, int SPAN, int NP>
 __device__ __forceinline__ void rotate_row(uint32_t tile, int rows, int r, int c0, int cstep,
-                                           const uint8_t* cos_row, const uint8_t* sin_row) {
-#pragma unroll 1
-  for (int c = c0; c < D / 16; c += cstep) {
-    const uint4 cv = ldg_v4(cos_row + c * 16);
-    const uint4 sv = ldg_v4(sin_row + c * 16);
+                                           const uint4 (&cv)[NP], const uint4 (&sv)[NP]) {
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    const int c = c0 + i * cstep;
     const uint32_t a1 = tile + swz_chunk_offset<SPAN>(rows, r, c);
     const uint32_t a2 = tile + swz_chunk_offset<SPAN>(rows, r, c + D / 16);
     const uint4 x1 = ld_shared_v4(a1);
     const uint4 x2 = ld_shared_v4(a2);
     const uint32_t xa[4] = {x1.x, x1.y, x1.z, x1.w};
     const uint32_t xb[4] = {x2.x, x2.y, x2.z, x2.w};
-    const uint32_t ca[4] = {cv.x, cv.y, cv.z, cv.w};
-    const uint32_t sa[4] = {sv.x, sv.y, sv.z, sv.w};
+    const uint32_t ca[4] = {cv[i].x, cv[i].y, cv[i].z, cv[i].w};
+    const uint32_t sa[4] = {sv[i].x, sv[i].y, sv[i].z, sv[i].w};
     uint32_t ya[4], yb[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 lo = unpack2<BF16>(xa[i]);
-      const float2 hi = unpack2<BF16>(xb[i]);
-      const float2 cc = unpack2<BF16>(ca[i]);
-      const float2 ss = unpack2<BF16>(sa[i]);
-      ya[i] = pack2<false>(lo.x * cc.x - hi.x * ss.x, lo.y * cc.y - hi.y * ss.y);
-      yb[i] = pack2<false>(hi.x * cc.x + lo.x * ss.x, hi.y * cc.y + lo.y * ss.y);
+    for (int e = 0; e < 4; ++e) {
+      const float2 lo = unpack2<BF16>(xa[e]);
+      const float2 hi = unpack2<BF16>(xb[e]);
+      const float2 cc = unpack2<BF16>(ca[e]);
+      const float2 ss = unpack2<BF16>(sa[e]);
+      ya[e] = pack2<false>(lo.x * cc.x - hi.x * ss.x, lo.y * cc.y - hi.y * ss.y);
+      yb[e] = pack2<false>(hi.x * cc.x + lo.x * ss.x, hi.y * cc.y + lo.y * ss.y);
     }
     st_shared_v4(a1, make_uint4(ya[0], ya[1], ya[2], ya[3]));
     st_shared_v4(a2, make_uint4(yb[0], yb[1], yb[2], yb[3]));
@@ -187,6 +212,7 @@ __global__ void __launch_bounds__(320, 1)
     for (int j = 0; j < n_kv; ++j) {
       ok = mbar_wait(BAR_SF(j & 1), (j >> 1) & 1, failed, 10);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+      if (tid == 0) DU_TRACE_EV(0, j);
       tc_fence_after();
       float s[BN];
       const uint32_t s_addr = tmem + lane_off + ((j & 1) ? S::TM_S1 : S::TM_S0);
@@ -216,8 +242,10 @@ __global__ void __launch_bounds__(320, 1)
         pk[c / 2] = pack2<BF16>(p0, p1);
       }
       if (j > 0) {
+        if (tid == 0) DU_TRACE_EV(1, j);
         ok = mbar_wait(BAR_OD, (j - 1) & 1, failed, 11);  // PV_{j-1} done: P free, O current
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        if (tid == 0) DU_TRACE_EV(2, j);
         tc_fence_after();
         const bool need = (m_new != m);
         if (__any_sync(0xffffffffu, need)) {
@@ -245,11 +273,13 @@ __global__ void __launch_bounds__(320, 1)
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(BAR_PF);
+      if (tid == 0) DU_TRACE_EV(3, j);
     }
     if (ok) {
       ok = mbar_wait(BAR_OD, (n_kv - 1) & 1, failed, 12);
       ok = __all_sync(0xffffffffu, ok);
     }
+    if (tid == 0) DU_TRACE_EV(4, 0);
     tc_fence_after();
     if (ok) {
       const float inv_l = 1.0f / l;
@@ -275,28 +305,47 @@ __global__ void __launch_bounds__(320, 1)
     const int rt = tid - 128;
     const uint8_t* cosb = static_cast<const uint8_t*>(p.cos);
     const uint8_t* sinb = static_cast<const uint8_t*>(p.sin);
-    constexpr int ROW_TAB = D;  // bytes per cos/sin table row (D/2 16-bit values)
-    if (mbar_wait(BAR_QF, 0, failed, 20)) {
+    constexpr int ROW_TAB = D;               // bytes per cos/sin table row (D/2 16-bit values)
+    constexpr int TPR = 128 / BN;            // threads per K row
+    constexpr int NPQ = (D / 16) < 8 ? (D / 16) : 8;  // chunk pairs per batch of a Q row
+    constexpr int NPK = (D / 16) / TPR;      // chunk pairs per thread of a K row (<= 8)
+    static_assert(NPK <= 8, "K rotation batch");
+    bool ok;
+    {
       const int pos = q0 + rt;
-      if (pos < T)
-        rotate_row<D, BF16, SPAN>(sbase + S::OFF_Q, BM, rt, 0, 1, cosb + static_cast<size_t>(pos) * ROW_TAB,
-                                  sinb + static_cast<size_t>(pos) * ROW_TAB);
-      fence_proxy_async_smem();
-      mbar_arrive(BAR_QR);
-      constexpr int TPR = 128 / BN;  // threads per K row
-      const int r = rt / TPR;
-      const int sub = rt % TPR;
-      for (int j = 0; j < n_kv; ++j) {
-        const int s = j % NS;
-        if (!mbar_wait(BAR_KF(s), (j / NS) & 1, failed, 21)) break;
-        const int kpos = j * BN + r;
-        if (kpos < T)
-          rotate_row<D, BF16, SPAN>(sbase + S::OFF_K + s * S::KV_BYTES, BN, r, sub, TPR,
-                                    cosb + static_cast<size_t>(kpos) * ROW_TAB,
-                                    sinb + static_cast<size_t>(kpos) * ROW_TAB);
-        fence_proxy_async_smem();
-        mbar_arrive(BAR_KR(s));
+      ok = true;
+#pragma unroll 1
+      for (int c0 = 0; c0 < D / 16; c0 += NPQ) {
+        uint4 cv[NPQ], sv[NPQ];
+        if (pos < T)
+          load_rope_row<NPQ>(cv, sv, cosb + static_cast<size_t>(pos) * ROW_TAB,
+                             sinb + static_cast<size_t>(pos) * ROW_TAB, c0, 1);
+        if (c0 == 0) ok = mbar_wait(BAR_QF, 0, failed, 20);
+        if (!ok) break;
+        if (pos < T) rotate_row<D, BF16, SPAN, NPQ>(sbase + S::OFF_Q, BM, rt, c0, 1, cv, sv);
       }
+      if (ok) {
+        fence_proxy_async_smem();
+        mbar_arrive(BAR_QR);
+      }
+    }
+    const int r = rt / TPR;
+    const int sub = rt % TPR;
+    for (int j = 0; ok && j < n_kv; ++j) {
+      const int s = j % NS;
+      const int kpos = j * BN + r;
+      uint4 cv[NPK], sv[NPK];
+      if (kpos < T)
+        load_rope_row<NPK>(cv, sv, cosb + static_cast<size_t>(kpos) * ROW_TAB,
+                           sinb + static_cast<size_t>(kpos) * ROW_TAB, sub, TPR);
+      if (rt == 0) DU_TRACE_EV(5, j);
+      if (!mbar_wait(BAR_KF(s), (j / NS) & 1, failed, 21)) break;
+      if (rt == 0) DU_TRACE_EV(6, j);
+      if (kpos < T)
+        rotate_row<D, BF16, SPAN, NPK>(sbase + S::OFF_K + s * S::KV_BYTES, BN, r, sub, TPR, cv, sv);
+      fence_proxy_async_smem();
+      mbar_arrive(BAR_KR(s));
+      if (rt == 0) DU_TRACE_EV(7, j);
     }
   } else if (warp == 8) {
     // ------------------------------------------------------------------ TMA producer
@@ -304,6 +353,7 @@ __global__ void __launch_bounds__(320, 1)
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
+      DU_TRACE_EV(11, 0);
       mbar_expect_tx(BAR_QF, S::Q_BYTES);
 #pragma unroll
       for (int blk = 0; blk < S::NBLK; ++blk)
@@ -313,6 +363,7 @@ __global__ void __launch_bounds__(320, 1)
         const int s = j % NS;
         const uint32_t ph = (j / NS) & 1;
         if (j >= NS && !mbar_wait(BAR_KE(s), ph ^ 1u, failed, 30)) break;
+        DU_TRACE_EV(12, j);
         mbar_expect_tx(BAR_KF(s), S::KV_BYTES);
 #pragma unroll
         for (int blk = 0; blk < S::NBLK; ++blk)
@@ -320,6 +371,7 @@ __global__ void __launch_bounds__(320, 1)
                       blk * (SPAN / 2), j * BN, kv_row);
         issued_k = j + 1;
         if (j >= NS && !mbar_wait(BAR_VE(s), ph ^ 1u, failed, 31)) break;
+        DU_TRACE_EV(13, j);
         mbar_expect_tx(BAR_VF(s), S::KV_BYTES);
 #pragma unroll
         for (int blk = 0; blk < S::NBLK; ++blk)
@@ -344,6 +396,7 @@ __global__ void __launch_bounds__(320, 1)
         if (j < n_kv) {
           const int s = j % NS;
           if (!mbar_wait(BAR_KR(s), (j / NS) & 1, failed, 41)) break;
+          DU_TRACE_EV(8, j);
           tc_fence_after();
           const uint32_t d_tmem = tmem + ((j & 1) ? S::TM_S1 : S::TM_S0);
 #pragma unroll
@@ -362,7 +415,9 @@ __global__ void __launch_bounds__(320, 1)
           const int jj = j - 1;
           const int s = jj % NS;
           if (!mbar_wait(BAR_PF, jj & 1, failed, 42)) break;
+          DU_TRACE_EV(9, jj);
           if (!mbar_wait(BAR_VF(s), (jj / NS) & 1, failed, 43)) break;
+          DU_TRACE_EV(10, jj);
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk) {
