@@ -42,6 +42,8 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 
 PREFILL = dict(B=2, H=32, Hkv=32, S=2048, D=64, base=10000.0)
 DECODE = dict(B=8, H=32, Hkv=32, L=2048, D=64, base=10000.0)
+# Long-context Llama-3-8B-shaped decode: the KV sequence is split across the ranks.
+DECODE_LONG = dict(B=4, H=32, Hkv=8, L=131072, D=128, base=500000.0)
 
 # Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) from the ncu captures
 # summarised under profiles/ (None until captured for the current kernel version).
@@ -303,6 +305,54 @@ def bench_decode(rank, device, stream, steps, warmup, peaks):
     }
 
 
+def bench_decode_long(dist, rank, world, device, stream, steps, warmup, peaks):
+    """Sequence-split decode: rank r holds keys [r L/N, (r+1) L/N) at their absolute positions;
+    per step: partial kernel(s) on the shard, one packed all-gather over NCCL, LSE merge."""
+    from dominusultra_b200 import dist as ddist
+    from dominusultra_b200 import decode_partial, merge_partials, precompute_rope_cos_sin
+
+    c = DECODE_LONG
+    B, H, Hkv, L, D = c["B"], c["H"], c["Hkv"], c["L"], c["D"]
+    a, b = ddist.kv_shard(L, world, rank)
+    Ls = b - a
+    g = torch.Generator(device=device).manual_seed(4000 + rank)
+    q = torch.randn(B, H, 1, D, generator=g, device=device).to(torch.bfloat16)
+    k = torch.randn(B, Hkv, Ls, D, generator=g, device=device).to(torch.bfloat16)
+    v = torch.randn(B, Hkv, Ls, D, generator=g, device=device).to(torch.bfloat16)
+    cos, sin = precompute_rope_cos_sin(L + 1, D, device, torch.bfloat16, c["base"])
+    rows = B * H
+    send = torch.empty(rows * (D + 1), dtype=torch.float32, device=device)
+    gathered = torch.empty(world * send.numel(), dtype=torch.float32, device=device)
+    o_view = send[: rows * D].view(B, H, D)
+    l_view = send[rows * D:].view(B, H)
+
+    def step(_i):
+        decode_partial(q, k, v, cos, sin, Hkv, q_pos=L, kv_pos_offset=a, out=o_view, lse=l_view)
+        if dist is not None:
+            dist.all_gather_into_tensor(gathered, send)
+            o_all, l_all = ddist.unpack_gathered(gathered, world, (B, H), D)
+        else:
+            o_all, l_all = o_view.unsqueeze(0), l_view.unsqueeze(0)
+        merge_partials(o_all, l_all, torch.bfloat16)
+
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    barrier(dist)
+    ms = time_region(step, steps, stream) / steps
+    ms = max_over_ranks(dist, ms, device)
+    total_bytes = decode_bytes(B, H, Hkv, L, D)
+    return {
+        "metric": "long-context decode KV-cache GB/s (whole job)",
+        "value": total_bytes / (ms / 1000.0) / 1e9, "unit": "GB/s", "ms_per_step": ms,
+        "scaling": "strong",
+        "config": {"workload": f"decode B{B} H{H} Hkv{Hkv} L{L} D{D} bf16 RoPE base 5e5, "
+                               f"KV sequence split over {world} GPU(s), one NCCL all-gather per step",
+                   "kv_bytes_per_gpu": total_bytes / world},
+        "per_gpu_hbm_frac": (total_bytes / world) / (ms / 1000.0) / 1e9 / peaks["hbm_gbs"],
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -311,6 +361,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-long-decode", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -389,6 +440,10 @@ def main():
             decode["value"] = world * decode_bytes(DECODE["B"], DECODE["H"], DECODE["Hkv"],
                                                    DECODE["L"], DECODE["D"]) / (dms / 1000.0) / 1e9
 
+    decode_long = None
+    if not args.no_long_decode:
+        decode_long = bench_decode_long(dist, rank, world, device, stream, args.steps, args.warmup, peaks)
+
     status = _lib.read_status(reset=True)
     line = None
     if rank == 0:
@@ -425,6 +480,8 @@ def main():
         }
         if decode is not None:
             line["decode"] = decode
+        if decode_long is not None:
+            line["decode_long"] = decode_long
         if not args.no_cpu_baseline:
             tf, t, cores = cpu_prefill_baseline(cfg)
             line["cpu_baseline"] = {

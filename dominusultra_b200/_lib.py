@@ -52,6 +52,7 @@ SIGNATURES = {
         [_vp, _vp, _i, _i, _i, _ll, _ll, _ll, _ll, _vp, _i, _vp, _vp],
     ),
     "du_decode_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _ll, _vp]),
+    "du_selftest_wait_timeout": (_i, [_i, _vp]),
     "du_read_status": (_i, [ctypes.POINTER(ctypes.c_uint), _i]),
 }
 

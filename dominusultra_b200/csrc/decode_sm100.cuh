@@ -13,8 +13,9 @@
 //    contiguous range of its cache; a persistent grid (resident CTAs only) walks the items;
 //  * a producer warp streams each item's keys in chunks of CK rows: K, V and the matching
 //    cos/sin table rows are contiguous in memory, so each chunk is four cp.async.bulk copies
-//    (no multicast) into a 4-stage shared-memory ring guarded by mbarriers, and it runs ahead
-//    across item boundaries;
+//    (no multicast) into a 3-stage shared-memory ring guarded by mbarriers, and it runs ahead
+//    across item boundaries; the item's query rows and the cos/sin row at the query position
+//    come the same way into a 2-entry header ring, so no consumer waits on a global load;
 //  * four consumer warps read the ring: D/16 lanes share one key row and each lane takes the
 //    two 16-byte chunks that are half-split RoPE partners (elements [8c, 8c+8) and
 //    [D/2 + 8c, D/2 + 8c + 8)), so the key rotation needs no shuffles; scores are reduced
@@ -55,7 +56,7 @@ struct DecodeParams {
 template <int D, int GT>
 struct DecodeShape {
   static constexpr int CK = 4096 / D;       // keys per ring stage
-  static constexpr int NSTG = 4;
+  static constexpr int NSTG = 3;            // 3 stages: three CTAs fit on an SM
   static constexpr int ROWB = 2 * D;        // bytes per K / V row
   static constexpr int TABB = D;            // bytes per cos / sin row (D/2 16-bit values)
   static constexpr int OFF_K = 0;
@@ -67,8 +68,15 @@ struct DecodeShape {
   static constexpr int KPW = 32 / LPR;      // keys per warp step
   static constexpr int NW = 4;              // consumer warps
   static constexpr int STEPS = CK / (NW * KPW);  // steps per warp per chunk
-  static constexpr int OFF_BAR = NSTG * STAGE;  // full[NSTG], empty[NSTG], merge[2], flag
-  static constexpr int OFF_MERGE = OFF_BAR + 8 * (2 * NSTG + 2) + 16;
+  // Per-item header ring (2 entries): the item's GT query rows, then the cos and sin rows at
+  // the query position, copied by the producer like the KV chunks.
+  static constexpr int NHDR = 2;
+  static constexpr int HDR_Q = GT * ROWB;
+  static constexpr int HDR = ((HDR_Q + 2 * TABB + 127) / 128) * 128;
+  static constexpr int OFF_HDR = NSTG * STAGE;
+  static constexpr int OFF_BAR = OFF_HDR + NHDR * HDR;  // full[NSTG], empty[NSTG], merge[2],
+                                                        // hfull[NHDR], hempty[NHDR], flag
+  static constexpr int OFF_MERGE = OFF_BAR + 8 * (2 * NSTG + 2 + 2 * NHDR) + 16;
   static constexpr int MERGE_BYTES = NW * GT * (D + 2) * 4;
   static constexpr int SMEM_BYTES = OFF_MERGE + MERGE_BYTES + 128;  // + alignment slack
   static constexpr int NTHREADS = 160;
@@ -87,7 +95,12 @@ __global__ void __launch_bounds__(160) decode_kernel(const DecodeParams p) {
   auto FULL = [&](int s) { return sbase + S::OFF_BAR + 8u * static_cast<uint32_t>(s); };
   auto EMPTY = [&](int s) { return sbase + S::OFF_BAR + 8u * static_cast<uint32_t>(NSTG + s); };
   auto MERGE = [&](int i) { return sbase + S::OFF_BAR + 8u * static_cast<uint32_t>(2 * NSTG + i); };
-  volatile int* failed = reinterpret_cast<volatile int*>(sgen + S::OFF_BAR + 8 * (2 * NSTG + 2));
+  auto HFULL = [&](int i) { return sbase + S::OFF_BAR + 8u * static_cast<uint32_t>(2 * NSTG + 2 + i); };
+  auto HEMPTY = [&](int i) {
+    return sbase + S::OFF_BAR + 8u * static_cast<uint32_t>(2 * NSTG + 2 + S::NHDR + i);
+  };
+  volatile int* failed =
+      reinterpret_cast<volatile int*>(sgen + S::OFF_BAR + 8 * (2 * NSTG + 2 + 2 * S::NHDR));
   float* sm_m = reinterpret_cast<float*>(sgen + S::OFF_MERGE);      // [NW][GT]
   float* sm_l = sm_m + S::NW * GT;                                   // [NW][GT]
   float* sm_acc = sm_l + S::NW * GT;                                 // [NW][GT][D]
@@ -101,6 +114,10 @@ __global__ void __launch_bounds__(160) decode_kernel(const DecodeParams p) {
     }
     mbar_init(MERGE(0), 128);  // the 128 consumer threads, once per work item
     mbar_init(MERGE(1), 128);
+    for (int i = 0; i < S::NHDR; ++i) {
+      mbar_init(HFULL(i), 1);
+      mbar_init(HEMPTY(i), 128);
+    }
     *failed = 0;
     mbar_fence_init();
     fence_proxy_async_smem();
@@ -117,12 +134,31 @@ __global__ void __launch_bounds__(160) decode_kernel(const DecodeParams p) {
     if (lane == 0) {
       int g = 0;  // chunk counter across items (ring stage / phase)
       bool ok = true;
-      for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x) {
+      int it = 0;
+      for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x, ++it) {
         const int unit = item / p.n_split;
         const int split = item - unit * p.n_split;
+        const int gch = unit % p.n_gchunk;
         const int bk = unit / p.n_gchunk;  // b * Hkv + kvh
         const int kbeg = split * p.keys_per_split;
         const int kend = min(p.L, kbeg + p.keys_per_split);
+        {
+          // Item header: query rows of the GT heads and the cos / sin rows at q_pos.
+          const int hs = it % S::NHDR;
+          if (it >= S::NHDR && !mbar_wait(HEMPTY(hs), ((it / S::NHDR) - 1) & 1, failed, 65)) {
+            ok = false;
+            break;
+          }
+          const int b = bk / p.Hkv;
+          const int h0 = (bk - b * p.Hkv) * p.G + gch * GT;
+          const uint32_t hd = sbase + S::OFF_HDR + hs * S::HDR;
+          const size_t trow = static_cast<size_t>(p.q_pos) * S::TABB;
+          mbar_expect_tx(HFULL(hs), static_cast<uint32_t>(S::HDR_Q + 2 * S::TABB));
+          bulk_load(hd, static_cast<const uint8_t*>(p.q) + (static_cast<size_t>(b) * p.Hq + h0) * S::ROWB,
+                    S::HDR_Q, HFULL(hs));
+          bulk_load(hd + S::HDR_Q, cosb + trow, S::TABB, HFULL(hs));
+          bulk_load(hd + S::HDR_Q + S::TABB, sinb + trow, S::TABB, HFULL(hs));
+        }
         for (int c0 = kbeg; c0 < kend; c0 += CK, ++g) {
           const int s = g % NSTG;
           if (g >= NSTG && !mbar_wait(EMPTY(s), ((g / NSTG) - 1) & 1, failed, 60)) {
@@ -142,6 +178,8 @@ __global__ void __launch_bounds__(160) decode_kernel(const DecodeParams p) {
       }
       // Drain: the last copies land before the CTA may exit.
       for (int j = (g > NSTG ? g - NSTG : 0); j < g; ++j) mbar_wait_drain(FULL(j % NSTG), (j / NSTG) & 1, 61);
+      for (int j = (it > S::NHDR ? it - S::NHDR : 0); j < it; ++j)
+        mbar_wait_drain(HFULL(j % S::NHDR), (j / S::NHDR) & 1, 66);
     }
     __syncwarp();
     return;
@@ -167,20 +205,21 @@ __global__ void __launch_bounds__(160) decode_kernel(const DecodeParams p) {
     const int kbeg = split * p.keys_per_split;
     const int kend = min(p.L, kbeg + p.keys_per_split);
 
-    // Rotated, pre-scaled query halves for this lane's 8 element pairs.
+    // Rotated, pre-scaled query halves for this lane's 8 element pairs (from the item header).
     float q1[GT][8], q2[GT][8];
     {
-      const size_t trow = static_cast<size_t>(p.q_pos) * S::TABB;
-      const uint4 cv = ldg_v4(cosb + trow + c * 16);
-      const uint4 sv = ldg_v4(sinb + trow + c * 16);
+      const int hs = it % S::NHDR;
+      ok = mbar_wait(HFULL(hs), (it / S::NHDR) & 1, failed, 67);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      const uint32_t hd = sbase + S::OFF_HDR + hs * S::HDR;
+      const uint4 cv = ld_shared_v4(hd + S::HDR_Q + c * 16);
+      const uint4 sv = ld_shared_v4(hd + S::HDR_Q + S::TABB + c * 16);
       const uint32_t ca[4] = {cv.x, cv.y, cv.z, cv.w};
       const uint32_t sa[4] = {sv.x, sv.y, sv.z, sv.w};
 #pragma unroll
       for (int gg = 0; gg < GT; ++gg) {
-        const uint8_t* qp =
-            static_cast<const uint8_t*>(p.q) + (static_cast<size_t>(b) * p.Hq + h0 + gg) * S::ROWB;
-        const uint4 x1 = ldg_v4(qp + c * 16);
-        const uint4 x2 = ldg_v4(qp + HALF * 2 + c * 16);
+        const uint4 x1 = ld_shared_v4(hd + gg * S::ROWB + c * 16);
+        const uint4 x2 = ld_shared_v4(hd + gg * S::ROWB + HALF * 2 + c * 16);
         const uint32_t xa[4] = {x1.x, x1.y, x1.z, x1.w};
         const uint32_t xb[4] = {x2.x, x2.y, x2.z, x2.w};
 #pragma unroll
@@ -195,6 +234,7 @@ __global__ void __launch_bounds__(160) decode_kernel(const DecodeParams p) {
           q2[gg][2 * i + 1] = (hi.y * cc.y + lo.y * ss.y) * p.scale_log2;
         }
       }
+      mbar_arrive(HEMPTY(hs));  // header consumed: the producer may reuse the entry
     }
 
     float m[GT], l[GT], acc[GT][16];

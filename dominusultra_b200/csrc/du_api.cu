@@ -18,6 +18,31 @@
 #include "prefill_sm100.cuh"
 #include "prefill_pair_sm100.cuh"
 
+namespace du {
+
+// One CTA waits on an mbarrier that nothing arrives at, bounded by timeout_ns: the timeout is
+// recorded in g_du_status (site 200) and the kernel returns.
+__global__ void selftest_wait_kernel(unsigned long long timeout_ns) {
+  __shared__ __align__(8) unsigned long long bar;
+  const uint32_t b = smem_u32(&bar);
+  if (threadIdx.x == 0) {
+    mbar_init(b, 1);
+    mbar_fence_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint64_t t0 = globaltimer();
+    while (!mbar_try_wait_sleep(b, 0, 1000u)) {
+      if (globaltimer() - t0 > timeout_ns) {
+        record_timeout(200);
+        break;
+      }
+    }
+  }
+}
+
+}  // namespace du
+
 namespace {
 
 thread_local std::string g_last_error;
@@ -178,22 +203,24 @@ struct DecodePlan {
   int keys_per_split;
 };
 
-// Work items are (unit, split); a persistent grid of resident CTAs walks them. Units are
-// (b, kv head, group chunk of GT query heads). When units alone cannot fill about four items
-// per resident CTA slot (two CTAs per SM by shared memory), each cache is split into
-// contiguous ranges whose length is a multiple of the kernel's chunk.
+// Work items are (unit, split); a persistent grid of resident CTAs walks them round-robin.
+// Units are (b, kv head, group chunk of GT query heads). When units alone cannot give each
+// resident CTA slot (three per SM) several items, each cache is split into contiguous ranges of
+// a whole number of the kernel's chunks (at least four chunks per split), so the per-CTA item
+// counts differ by at most one item of a few chunks.
 DecodePlan plan_decode(int B, int Hq, int Hkv, int L, int D) {
   DecodePlan pl{};
   const int G = Hq / Hkv;
   pl.GT = (G % 4 == 0) ? 4 : ((G % 2 == 0) ? 2 : 1);
   pl.n_gchunk = G / pl.GT;
   const long long units = static_cast<long long>(B) * Hkv * pl.n_gchunk;
-  const long long slots = static_cast<long long>(sm_count()) * 2;
+  const long long slots = static_cast<long long>(sm_count()) * 3;
   const int chunk = 4096 / D;  // DecodeShape<D>::CK
+  const long long min_keys = 4LL * chunk;
   long long ns = 1;
-  if (units < slots) {
-    ns = (4 * slots + units - 1) / units;
-    const long long max_split = (L + 2 * chunk - 1) / (2 * chunk);  // >= 2 chunks per split
+  if (units < 8 * slots) {
+    ns = (8 * slots + units - 1) / units;
+    const long long max_split = (L + min_keys - 1) / min_keys;
     if (ns > max_split) ns = max_split;
     if (ns < 1) ns = 1;
   }
@@ -516,6 +543,17 @@ int du_trace_read(long long* out) {
   return e == cudaSuccess ? DU_OK : DU_ERR_CUDA;
 }
 #endif
+
+int du_selftest_wait_timeout(int timeout_us, void* stream) {
+  g_last_error.clear();
+  if (timeout_us < 1 || timeout_us > 1000000)
+    return fail(DU_ERR_INVALID, "timeout_us must be in [1, 1000000]");
+  du::selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<unsigned long long>(timeout_us) * 1000ull);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "selftest launch");
+  return DU_OK;
+}
 
 int du_read_status(unsigned int* words4, int reset) {
   g_last_error.clear();

@@ -114,6 +114,14 @@ int du_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, c
                       int dtype, float scale, long long rope_positions, void* stream);
 
 /*
+ * Failure-detection self-test (no counterpart in the reference): launches one CTA whose
+ * bounded wait can never complete -- an mbarrier nothing arrives at -- with a limit of
+ * timeout_us microseconds (1..1000000). The kernel records DU_ERR_TIMEOUT in the status words
+ * (wait site 200) and returns; nothing faults or hangs, and the context stays usable.
+ */
+int du_selftest_wait_timeout(int timeout_us, void* stream);
+
+/*
  * Read the device status words written when a bounded wait expires:
  * words[0] = error code (0 ok, DU_ERR_TIMEOUT), [1] wait site, [2..3] block index.
  * Synchronises the current device. reset != 0 clears them. Returns DU_OK or DU_ERR_CUDA.
