@@ -353,6 +353,57 @@ def bench_decode_long(dist, rank, world, device, stream, steps, warmup, peaks):
     }
 
 
+def reference_gpu_baseline(device, steps, warmup):
+    """The reference's own Triton kernels (installed unmodified in baseline/_ref) on this GPU,
+    on the headline prefill and decode configurations; compile and autotune excluded by
+    warm-up. Reported beside the CPU baseline; 'unavailable' with the reason if they cannot
+    run here."""
+    import importlib.util
+
+    path = ROOT / "baseline" / "_ref" / "dominus_ultra.py"
+    if not path.exists():
+        return {"unavailable": "reference not installed in baseline/_ref"}
+    try:
+        spec = importlib.util.spec_from_file_location("dominus_ultra_reference", path)
+        ref = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(ref)
+        from dominusultra_b200 import precompute_rope_cos_sin
+
+        res = {"impl": "reference Triton kernels from baseline/_ref (unmodified)"}
+        c = PREFILL
+        B, H, Hkv, S, D = c["B"], c["H"], c["Hkv"], c["S"], c["D"]
+        g = torch.Generator(device=device).manual_seed(99)
+        q = torch.randn(B, H, S, D, generator=g, device=device).to(torch.bfloat16)
+        k = torch.randn(B, Hkv, S, D, generator=g, device=device).to(torch.bfloat16)
+        v = torch.randn(B, Hkv, S, D, generator=g, device=device).to(torch.bfloat16)
+        cos, sin = precompute_rope_cos_sin(S, D, device, torch.bfloat16, c["base"])
+        stream = torch.cuda.current_stream(device)
+        fn = lambda i: ref.dominus_ultra_prefill(q, k, v, cos, sin, Hkv)  # noqa: E731
+        for i in range(max(warmup, 3)):
+            fn(i)
+        torch.cuda.synchronize()
+        ms = time_region(fn, steps, stream) / steps
+        res["prefill"] = {"value": prefill_flops(B, H, S, D) / (ms / 1000.0) / 1e12,
+                          "unit": "TFLOP/s", "ms_per_step": ms}
+        c = DECODE
+        B, H, Hkv, L, D = c["B"], c["H"], c["Hkv"], c["L"], c["D"]
+        q = torch.randn(B, H, 1, D, generator=g, device=device).to(torch.bfloat16)
+        k = torch.randn(B, Hkv, L, D, generator=g, device=device).to(torch.bfloat16)
+        v = torch.randn(B, Hkv, L, D, generator=g, device=device).to(torch.bfloat16)
+        cos, sin = precompute_rope_cos_sin(L + 1, D, device, torch.bfloat16, c["base"])
+        fn = lambda i: ref.dominus_ultra_decode(q, k, v, cos, sin, Hkv)  # noqa: E731
+        for i in range(max(warmup, 3)):
+            fn(i)
+        torch.cuda.synchronize()
+        ms = time_region(fn, steps, stream) / steps
+        res["decode"] = {"value": decode_bytes(B, H, Hkv, L, D) / (ms / 1000.0) / 1e9,
+                         "unit": "GB/s", "ms_per_step": ms,
+                         "note": "no L2 flush between steps (KV is 134 MB, just above L2)"}
+        return res
+    except Exception as e:  # the reference's kernels failing here is reported, not fatal
+        return {"unavailable": f"{type(e).__name__}: {str(e).splitlines()[0][:200]}"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -362,6 +413,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-long-decode", action="store_true")
+    ap.add_argument("--no-reference-gpu", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -482,6 +534,8 @@ def main():
             line["decode"] = decode
         if decode_long is not None:
             line["decode_long"] = decode_long
+        if not args.no_reference_gpu:
+            line["reference_gpu"] = reference_gpu_baseline(device, min(args.steps, 20), args.warmup)
         if not args.no_cpu_baseline:
             tf, t, cores = cpu_prefill_baseline(cfg)
             line["cpu_baseline"] = {

@@ -114,12 +114,39 @@ def _aligned(t: torch.Tensor) -> torch.Tensor:
     return t if t.data_ptr() % 16 == 0 else t.clone()
 
 
-def _stream(device: torch.device) -> ctypes.c_void_p:
-    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
 
 
-def _ptr(t: Optional[torch.Tensor]) -> ctypes.c_void_p:
-    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+def _ptr(t: Optional[torch.Tensor]) -> int:
+    return 0 if t is None else t.data_ptr()
+
+
+class _OnDevice:
+    """Make `device` current only when it is not already (the common case costs one call)."""
+
+    __slots__ = ("index", "prev")
+
+    def __init__(self, device: torch.device):
+        self.index = device.index if device.index is not None else torch.cuda.current_device()
+        self.prev = None
+
+    def __enter__(self):
+        cur = torch.cuda.current_device()
+        if cur != self.index:
+            self.prev = cur
+            torch.cuda.set_device(self.index)
+        return self
+
+    def __exit__(self, *exc):
+        if self.prev is not None:
+            torch.cuda.set_device(self.prev)
+        return False
+
+
+# Decode workspace per (device, stream): reused across calls, since kernels on one stream run
+# in order; grown on demand.
+_WORKSPACES = {}
 
 
 def dominus_ultra_prefill(
@@ -174,7 +201,7 @@ def dominus_ultra_prefill(
     out = torch.empty_like(q)
     lse = torch.empty((B, Hq, T), dtype=torch.float32, device=q.device)
     scale = 1.0 / (D**0.5)
-    with torch.cuda.device(q.device):
+    with _OnDevice(q.device):
         rc = lib.du_prefill(
             _ptr(q), _ptr(k), _ptr(v), _ptr(cos), _ptr(sin), _ptr(out), _ptr(lse),
             B, Hq, KvH, T, D, _dtype_code(q.dtype), scale,
@@ -184,11 +211,16 @@ def dominus_ultra_prefill(
     return out, lse
 
 
-def _workspace(B: int, Hq: int, Hkv: int, L: int, D: int, device) -> Tuple[Optional[torch.Tensor], int]:
+def _workspace(B: int, Hq: int, Hkv: int, L: int, D: int, device, stream: int):
     nbytes = int(_lib.load().du_decode_workspace_size(B, Hq, Hkv, L, D))
     if nbytes == 0:
-        return None, 0
-    return torch.empty(nbytes, dtype=torch.uint8, device=device), nbytes
+        return 0, 0
+    key = (device.index, stream)
+    ws = _WORKSPACES.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _WORKSPACES[key] = ws
+    return ws.data_ptr(), ws.numel()
 
 
 def dominus_ultra_decode(
@@ -242,12 +274,13 @@ def dominus_ultra_decode(
     q_new, k_cache, v_cache, cos, sin = (_aligned(t) for t in (q_new, k_cache, v_cache, cos, sin))
     out = torch.empty_like(q_new).squeeze(2)
     scale = 1.0 / (D**0.5)
-    with torch.cuda.device(q_new.device):
-        ws, nbytes = _workspace(B, Hq, KvH, past_T, D, q_new.device)
+    with _OnDevice(q_new.device):
+        stream = _stream(q_new.device)
+        ws, nbytes = _workspace(B, Hq, KvH, past_T, D, q_new.device, stream)
         rc = lib.du_decode(
             _ptr(q_new), _ptr(k_cache), _ptr(v_cache), _ptr(cos), _ptr(sin), _ptr(out),
             B, Hq, KvH, past_T, D, _dtype_code(q_new.dtype), scale,
-            min(cos.shape[0], sin.shape[0]), _ptr(ws), nbytes, _stream(q_new.device),
+            min(cos.shape[0], sin.shape[0]), ws, nbytes, stream,
         )
     _lib.check(rc, "du_decode")
     return out.unsqueeze(2)
@@ -283,13 +316,14 @@ def decode_partial(
         out = torch.empty((B, Hq, D), dtype=torch.float32, device=q_new.device)
     if lse is None:
         lse = torch.empty((B, Hq), dtype=torch.float32, device=q_new.device)
-    with torch.cuda.device(q_new.device):
-        ws, nbytes = _workspace(B, Hq, KvH, L, D, q_new.device)
+    with _OnDevice(q_new.device):
+        stream = _stream(q_new.device)
+        ws, nbytes = _workspace(B, Hq, KvH, L, D, q_new.device, stream)
         rc = lib.du_decode_partial(
             _ptr(q_new), _ptr(k_shard), _ptr(v_shard), _ptr(cos), _ptr(sin), _ptr(out), _ptr(lse),
             B, Hq, KvH, L, D, _dtype_code(q_new.dtype), 1.0 / (D**0.5),
             int(q_pos), int(kv_pos_offset), min(cos.shape[0], sin.shape[0]),
-            _ptr(ws), nbytes, _stream(q_new.device),
+            ws, nbytes, stream,
         )
     _lib.check(rc, "du_decode_partial")
     return out, lse
@@ -324,7 +358,7 @@ def merge_partials(
     out = torch.empty((*row_shape, D), dtype=out_dtype, device=o_parts.device)
     lse = torch.empty(row_shape, dtype=torch.float32, device=o_parts.device) if with_lse else None
     lib = _lib.load()
-    with torch.cuda.device(o_parts.device):
+    with _OnDevice(o_parts.device):
         rc = lib.du_merge_partials(
             _ptr(o2), _ptr(l2), R, rows, D, o2.stride(0), o2.stride(1), l2.stride(0), l2.stride(1),
             _ptr(out), _dtype_code(out_dtype), _ptr(lse), _stream(o_parts.device),

@@ -16,11 +16,13 @@
 //    (no multicast) into a 3-stage shared-memory ring guarded by mbarriers, and it runs ahead
 //    across item boundaries; the item's query rows and the cos/sin row at the query position
 //    come the same way into a 2-entry header ring, so no consumer waits on a global load;
-//  * four consumer warps read the ring: D/16 lanes share one key row and each lane takes the
-//    two 16-byte chunks that are half-split RoPE partners (elements [8c, 8c+8) and
-//    [D/2 + 8c, D/2 + 8c + 8)), so the key rotation needs no shuffles; scores are reduced
-//    across the D/16 lanes with xor-shuffles; the online softmax runs per lane group in the
-//    log2 domain, one rescale per chunk;
+//  * four consumer warps read the ring: a few lanes share one key row and each lane takes
+//    whole half-split RoPE partner chunks (elements [8c, 8c+8) and [D/2 + 8c, D/2 + 8c + 8)),
+//    so the key rotation needs no shuffles; it runs two elements per instruction in the input
+//    dtype (as the reference rotates in the input dtype), the rotated key and V are widened to
+//    fp32 and the dot products / P V sums use packed f32x2 FMAs; scores are reduced across the
+//    lanes of a row with xor-shuffles; the online softmax runs per lane group in the log2
+//    domain and moves its reference max only when a score exceeds it by 2^8;
 //  * at the end of an item the lane groups and warps are merged; with more than one split per
 //    row, each split writes an fp32 partial (out normalised over the split, natural-log LSE)
 //    and merge_kernel combines them.
@@ -64,9 +66,12 @@ struct DecodeShape {
   static constexpr int OFF_C = 2 * CK * ROWB;
   static constexpr int OFF_S = OFF_C + CK * TABB;
   static constexpr int STAGE = OFF_S + CK * TABB;  // 24 KB
-  static constexpr int LPR = D / 16;        // lanes per key row
-  static constexpr int KPW = 32 / LPR;      // keys per warp step
-  static constexpr int NW = 4;              // consumer warps
+  // Each lane takes PPL half-split chunk pairs (2 x 8 elements each) of a key row; smaller
+  // groups of heads leave room in registers for two pairs, which halves the lanes per row.
+  static constexpr int PPL = (GT >= 4 || D < 32) ? 1 : 2;
+  static constexpr int LPR = (D / 16) / PPL;     // lanes per key row
+  static constexpr int KPW = 32 / LPR;           // keys per warp step
+  static constexpr int NW = 4;                   // consumer warps
   static constexpr int STEPS = CK / (NW * KPW);  // steps per warp per chunk
   // Per-item header ring (2 entries): the item's GT query rows, then the cos and sin rows at
   // the query position, copied by the producer like the KV chunks.
@@ -80,11 +85,11 @@ struct DecodeShape {
   static constexpr int MERGE_BYTES = NW * GT * (D + 2) * 4;
   static constexpr int SMEM_BYTES = OFF_MERGE + MERGE_BYTES + 128;  // + alignment slack
   static constexpr int NTHREADS = 160;
-  static_assert(STEPS == 2, "chunk geometry");
+  static_assert(STEPS >= 1 && CK % (NW * KPW) == 0, "chunk geometry");
 };
 
 template <int D, bool BF16, int GT>
-__global__ void __launch_bounds__(160) decode_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(160, (GT >= 4) ? 1 : 2) decode_kernel(const DecodeParams p) {
   using S = DecodeShape<D, GT>;
   constexpr int LPR = S::LPR, KPW = S::KPW, NSTG = S::NSTG, CK = S::CK, HALF = D / 2;
 
@@ -186,11 +191,9 @@ __global__ void __launch_bounds__(160) decode_kernel(const DecodeParams p) {
   }
 
   // -------------------------------------------------------------------- consumers (warps 0..3)
-  const int kg = lane / LPR;
-  const int c = lane % LPR;
-  // Lane groups of odd keys read the two partner chunks in the opposite order, so the eight
-  // lanes of a shared-memory phase touch eight distinct 16-byte bank groups when D = 64.
-  const bool swap_order = (kg & 1) != 0;
+  constexpr int PPL = S::PPL;
+  const int kg = lane / LPR;       // key slot within a warp step
+  const int sub = lane % LPR;      // this lane's chunk pairs: sub * PPL + i, i < PPL
   int g = 0;
   bool ok = true;
   int it = 0;  // items processed by this CTA (merge-barrier phase)
@@ -205,45 +208,51 @@ __global__ void __launch_bounds__(160) decode_kernel(const DecodeParams p) {
     const int kbeg = split * p.keys_per_split;
     const int kend = min(p.L, kbeg + p.keys_per_split);
 
-    // Rotated, pre-scaled query halves for this lane's 8 element pairs (from the item header).
-    float q1[GT][8], q2[GT][8];
+    // Rotated, pre-scaled query pairs (log2 domain) for this lane's chunk pairs, from the header.
+    uint64_t q1[GT][PPL][4], q2[GT][PPL][4];
     {
       const int hs = it % S::NHDR;
       ok = mbar_wait(HFULL(hs), (it / S::NHDR) & 1, failed, 67);
       if (!__all_sync(0xffffffffu, ok)) break;
       const uint32_t hd = sbase + S::OFF_HDR + hs * S::HDR;
-      const uint4 cv = ld_shared_v4(hd + S::HDR_Q + c * 16);
-      const uint4 sv = ld_shared_v4(hd + S::HDR_Q + S::TABB + c * 16);
-      const uint32_t ca[4] = {cv.x, cv.y, cv.z, cv.w};
-      const uint32_t sa[4] = {sv.x, sv.y, sv.z, sv.w};
 #pragma unroll
-      for (int gg = 0; gg < GT; ++gg) {
-        const uint4 x1 = ld_shared_v4(hd + gg * S::ROWB + c * 16);
-        const uint4 x2 = ld_shared_v4(hd + gg * S::ROWB + HALF * 2 + c * 16);
-        const uint32_t xa[4] = {x1.x, x1.y, x1.z, x1.w};
-        const uint32_t xb[4] = {x2.x, x2.y, x2.z, x2.w};
+      for (int i = 0; i < PPL; ++i) {
+        const int c = sub * PPL + i;
+        const uint4 cv = ld_shared_v4(hd + S::HDR_Q + c * 16);
+        const uint4 sv = ld_shared_v4(hd + S::HDR_Q + S::TABB + c * 16);
+        const uint32_t ca[4] = {cv.x, cv.y, cv.z, cv.w};
+        const uint32_t sa[4] = {sv.x, sv.y, sv.z, sv.w};
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 lo = unpack2<BF16>(xa[i]);
-          const float2 hi = unpack2<BF16>(xb[i]);
-          const float2 cc = unpack2<BF16>(ca[i]);
-          const float2 ss = unpack2<BF16>(sa[i]);
-          q1[gg][2 * i] = (lo.x * cc.x - hi.x * ss.x) * p.scale_log2;
-          q1[gg][2 * i + 1] = (lo.y * cc.y - hi.y * ss.y) * p.scale_log2;
-          q2[gg][2 * i] = (hi.x * cc.x + lo.x * ss.x) * p.scale_log2;
-          q2[gg][2 * i + 1] = (hi.y * cc.y + lo.y * ss.y) * p.scale_log2;
+        for (int gg = 0; gg < GT; ++gg) {
+          const uint4 x1 = ld_shared_v4(hd + gg * S::ROWB + c * 16);
+          const uint4 x2 = ld_shared_v4(hd + gg * S::ROWB + HALF * 2 + c * 16);
+          const uint32_t xa[4] = {x1.x, x1.y, x1.z, x1.w};
+          const uint32_t xb[4] = {x2.x, x2.y, x2.z, x2.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 lo = unpack2<BF16>(xa[e]);
+            const float2 hi = unpack2<BF16>(xb[e]);
+            const float2 cc = unpack2<BF16>(ca[e]);
+            const float2 ss = unpack2<BF16>(sa[e]);
+            const float sc = p.scale_log2;
+            q1[gg][i][e] = f2((lo.x * cc.x - hi.x * ss.x) * sc, (lo.y * cc.y - hi.y * ss.y) * sc);
+            q2[gg][i][e] = f2((hi.x * cc.x + lo.x * ss.x) * sc, (hi.y * cc.y + lo.y * ss.y) * sc);
+          }
         }
       }
       mbar_arrive(HEMPTY(hs));  // header consumed: the producer may reuse the entry
     }
 
-    float m[GT], l[GT], acc[GT][16];
+    float m[GT], l[GT];
+    uint64_t acc[GT][PPL][8];  // f32 pairs: [0,4) first-half chunk, [4,8) second-half chunk
 #pragma unroll
     for (int gg = 0; gg < GT; ++gg) {
       m[gg] = -1e30f;
       l[gg] = 0.f;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) acc[gg][i] = 0.f;
+      for (int i = 0; i < PPL; ++i)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[gg][i][e] = f2(0.f, 0.f);
     }
 
     for (int c0 = kbeg; ok && c0 < kend; c0 += CK, ++g) {
@@ -256,91 +265,97 @@ __global__ void __launch_bounds__(160) decode_kernel(const DecodeParams p) {
       const int n = min(CK, kend - c0);
       const uint32_t st = sbase + s * S::STAGE;
       float sc[S::STEPS][GT];
-      float vf[S::STEPS][16];
+      uint4 vx[S::STEPS][PPL][2];
 #pragma unroll
       for (int u = 0; u < S::STEPS; ++u) {
         const int key = warp * (CK / S::NW) + u * KPW + kg;  // row within the chunk
         const bool valid = key < n;
-        uint4 kx1 = make_uint4(0, 0, 0, 0), kx2 = kx1, vx1 = kx1, vx2 = kx1, cv = kx1, sv = kx1;
-        if (valid) {
-          const uint32_t kr = st + S::OFF_K + key * S::ROWB;
-          const uint32_t vr = st + S::OFF_V + key * S::ROWB;
-          const int ca = swap_order ? c + LPR : c;
-          const int cb = swap_order ? c : c + LPR;
-          const uint4 ka = ld_shared_v4(kr + ca * 16);
-          const uint4 kb = ld_shared_v4(kr + cb * 16);
-          const uint4 va = ld_shared_v4(vr + ca * 16);
-          const uint4 vb = ld_shared_v4(vr + cb * 16);
-          kx1 = swap_order ? kb : ka;
-          kx2 = swap_order ? ka : kb;
-          vx1 = swap_order ? vb : va;
-          vx2 = swap_order ? va : vb;
-          cv = ld_shared_v4(st + S::OFF_C + key * S::TABB + c * 16);
-          sv = ld_shared_v4(st + S::OFF_S + key * S::TABB + c * 16);
-        }
-        const uint32_t xa[4] = {kx1.x, kx1.y, kx1.z, kx1.w};
-        const uint32_t xb[4] = {kx2.x, kx2.y, kx2.z, kx2.w};
-        const uint32_t cca[4] = {cv.x, cv.y, cv.z, cv.w};
-        const uint32_t ssa[4] = {sv.x, sv.y, sv.z, sv.w};
-        float k1[8], k2[8];
+        uint64_t dot[GT];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 lo = unpack2<BF16>(xa[i]);
-          const float2 hi = unpack2<BF16>(xb[i]);
-          const float2 cc = unpack2<BF16>(cca[i]);
-          const float2 ss = unpack2<BF16>(ssa[i]);
-          k1[2 * i] = lo.x * cc.x - hi.x * ss.x;
-          k1[2 * i + 1] = lo.y * cc.y - hi.y * ss.y;
-          k2[2 * i] = hi.x * cc.x + lo.x * ss.x;
-          k2[2 * i + 1] = hi.y * cc.y + lo.y * ss.y;
+        for (int gg = 0; gg < GT; ++gg) dot[gg] = f2(0.f, 0.f);
+#pragma unroll
+        for (int i = 0; i < PPL; ++i) {
+          const int c = sub * PPL + i;
+          uint4 k1 = make_uint4(0, 0, 0, 0), k2 = k1, cv = k1, sv = k1;
+          vx[u][i][0] = vx[u][i][1] = k1;
+          if (valid) {
+            const uint32_t kr = st + S::OFF_K + key * S::ROWB;
+            const uint32_t vr = st + S::OFF_V + key * S::ROWB;
+            k1 = ld_shared_v4(kr + c * 16);
+            k2 = ld_shared_v4(kr + HALF * 2 + c * 16);
+            vx[u][i][0] = ld_shared_v4(vr + c * 16);
+            vx[u][i][1] = ld_shared_v4(vr + HALF * 2 + c * 16);
+            cv = ld_shared_v4(st + S::OFF_C + key * S::TABB + c * 16);
+            sv = ld_shared_v4(st + S::OFF_S + key * S::TABB + c * 16);
+          }
+          const uint32_t ka[4] = {k1.x, k1.y, k1.z, k1.w};
+          const uint32_t kb[4] = {k2.x, k2.y, k2.z, k2.w};
+          const uint32_t ca[4] = {cv.x, cv.y, cv.z, cv.w};
+          const uint32_t sa[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            // Rotate two elements per instruction in the input dtype, then widen to fp32.
+            uint32_t r1, r2;
+            rope_rotate2<BF16>(ka[e], kb[e], ca[e], sa[e], r1, r2);
+            const uint64_t k1f = widen2<BF16>(r1);
+            const uint64_t k2f = widen2<BF16>(r2);
+#pragma unroll
+            for (int gg = 0; gg < GT; ++gg)
+              dot[gg] = f2_fma(q2[gg][i][e], k2f, f2_fma(q1[gg][i][e], k1f, dot[gg]));
+          }
         }
 #pragma unroll
         for (int gg = 0; gg < GT; ++gg) {
-          float d = 0.f;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) d = fmaf(q1[gg][i], k1[i], fmaf(q2[gg][i], k2[i], d));
+          const float2 dd = f2_split(dot[gg]);
+          float d = dd.x + dd.y;
 #pragma unroll
           for (int o = LPR / 2; o >= 1; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
           sc[u][gg] = valid ? d : -INFINITY;
-        }
-        const uint32_t va4[4] = {vx1.x, vx1.y, vx1.z, vx1.w};
-        const uint32_t vb4[4] = {vx2.x, vx2.y, vx2.z, vx2.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 a = unpack2<BF16>(va4[i]);
-          const float2 bb = unpack2<BF16>(vb4[i]);
-          vf[u][2 * i] = a.x;
-          vf[u][2 * i + 1] = a.y;
-          vf[u][8 + 2 * i] = bb.x;
-          vf[u][8 + 2 * i + 1] = bb.y;
         }
       }
       // The stage's shared memory has been read into registers: release it to the producer.
       __syncwarp();
       if (lane == 0) mbar_arrive(EMPTY(s));
 #pragma unroll
-      for (int gg = 0; gg < GT; ++gg) {
-        float mb = sc[0][gg];
+      for (int u = 0; u < S::STEPS; ++u) {
+        uint64_t vf[PPL][8];
 #pragma unroll
-        for (int u = 1; u < S::STEPS; ++u) mb = fmaxf(mb, sc[u][gg]);
-        const float mn = fmaxf(m[gg], mb);
-        const float alpha = ex2(m[gg] - mn);
-        l[gg] *= alpha;
+        for (int i = 0; i < PPL; ++i) {
+          const uint32_t va[4] = {vx[u][i][0].x, vx[u][i][0].y, vx[u][i][0].z, vx[u][i][0].w};
+          const uint32_t vb[4] = {vx[u][i][1].x, vx[u][i][1].y, vx[u][i][1].z, vx[u][i][1].w};
 #pragma unroll
-        for (int i = 0; i < 16; ++i) acc[gg][i] *= alpha;
-#pragma unroll
-        for (int u = 0; u < S::STEPS; ++u) {
-          const float pe = ex2(sc[u][gg] - mn);
-          l[gg] += pe;
-#pragma unroll
-          for (int i = 0; i < 16; ++i) acc[gg][i] = fmaf(pe, vf[u][i], acc[gg][i]);
+          for (int e = 0; e < 4; ++e) {
+            vf[i][e] = widen2<BF16>(va[e]);
+            vf[i][4 + e] = widen2<BF16>(vb[e]);
+          }
         }
-        m[gg] = mn;
+#pragma unroll
+        for (int gg = 0; gg < GT; ++gg) {
+          const float sv_ = sc[u][gg];
+          // Lazy rescale: move the reference max only when the score exceeds it by 2^8.
+          if (sv_ > m[gg] + 8.0f) {
+            const float alpha = ex2(m[gg] - sv_);
+            const uint64_t a2 = f2(alpha, alpha);
+            l[gg] *= alpha;
+#pragma unroll
+            for (int i = 0; i < PPL; ++i)
+#pragma unroll
+              for (int e = 0; e < 8; ++e) acc[gg][i][e] = f2_mul(acc[gg][i][e], a2);
+            m[gg] = sv_;
+          }
+          const float pe = ex2(sv_ - m[gg]);
+          l[gg] += pe;
+          const uint64_t p2 = f2(pe, pe);
+#pragma unroll
+          for (int i = 0; i < PPL; ++i)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[gg][i][e] = f2_fma(p2, vf[i][e], acc[gg][i][e]);
+        }
       }
     }
     if (!ok) break;
 
-    // Merge the KPW key groups of the warp (butterfly over lanes with the same chunk index).
+    // Merge the KPW key groups of the warp (butterfly over lanes with the same chunk pairs).
 #pragma unroll
     for (int o = LPR; o < 32; o <<= 1) {
 #pragma unroll
@@ -351,26 +366,38 @@ __global__ void __launch_bounds__(160) decode_kernel(const DecodeParams p) {
         const float wa = ex2(m[gg] - mn);
         const float wb = ex2(mo - mn);
         l[gg] = l[gg] * wa + lo * wb;
+        const uint64_t wa2 = f2(wa, wa), wb2 = f2(wb, wb);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float ao = __shfl_xor_sync(0xffffffffu, acc[gg][i], o);
-          acc[gg][i] = acc[gg][i] * wa + ao * wb;
-        }
+        for (int i = 0; i < PPL; ++i)
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float2 a = f2_split(acc[gg][i][e]);
+            const uint64_t ao = f2(__shfl_xor_sync(0xffffffffu, a.x, o), __shfl_xor_sync(0xffffffffu, a.y, o));
+            acc[gg][i][e] = f2_fma(ao, wb2, f2_mul(acc[gg][i][e], wa2));
+          }
         m[gg] = mn;
       }
     }
     if (kg == 0) {
 #pragma unroll
       for (int gg = 0; gg < GT; ++gg) {
-        if (c == 0) {
+        if (sub == 0) {
           sm_m[warp * GT + gg] = m[gg];
           sm_l[warp * GT + gg] = l[gg];
         }
         float* a = sm_acc + (warp * GT + gg) * D;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          a[8 * c + i] = acc[gg][i];
-          a[HALF + 8 * c + i] = acc[gg][8 + i];
+        for (int i = 0; i < PPL; ++i) {
+          const int c = sub * PPL + i;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 x1 = f2_split(acc[gg][i][e]);
+            const float2 x2 = f2_split(acc[gg][i][4 + e]);
+            a[8 * c + 2 * e] = x1.x;
+            a[8 * c + 2 * e + 1] = x1.y;
+            a[HALF + 8 * c + 2 * e] = x2.x;
+            a[HALF + 8 * c + 2 * e + 1] = x2.y;
+          }
         }
       }
     }
@@ -414,28 +441,61 @@ __global__ void __launch_bounds__(160) decode_kernel(const DecodeParams p) {
 
 // LSE-weighted merge of R partials per row: lse = log(sum_r exp(lse_r)),
 // out = sum_r exp(lse_r - lse) * o_r. Rows whose partials all have lse = -inf produce zeros and
-// lse = -inf. out_kind: 0 fp16, 1 bf16, 2 fp32.
-__global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ o_parts,
+// lse = -inf. out_kind: 0 fp16, 1 bf16, 2 fp32. One CTA per row: the R weights are computed in
+// parallel into shared memory (R <= MERGE_MAX_R), then each thread sums its columns with
+// independent loads.
+constexpr int MERGE_MAX_R = 4096;
+
+__global__ void __launch_bounds__(128) merge_kernel(const float* __restrict__ o_parts,
                                                     const float* __restrict__ lse_parts, int R,
                                                     int D, long long o_sr, long long o_srow,
                                                     long long l_sr, long long l_srow, void* out,
                                                     int out_kind, float* lse_out) {
+  __shared__ float w[MERGE_MAX_R];
+  __shared__ float red[4];
+  __shared__ float s_m, s_w;
   const long long row = blockIdx.x;
-  float M = -INFINITY;
-  for (int r = 0; r < R; ++r) M = fmaxf(M, lse_parts[r * l_sr + row * l_srow]);
-  float W = 0.f;
-  if (M != -INFINITY) {
-    for (int r = 0; r < R; ++r) W += expf(lse_parts[r * l_sr + row * l_srow] - M);
+  const int tid = threadIdx.x;
+  float mx = -INFINITY;
+  for (int r = tid; r < R; r += 128) {
+    const float v = lse_parts[r * l_sr + row * l_srow];
+    w[r] = v;
+    mx = fmaxf(mx, v);
   }
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
-    float A = 0.f;
-    if (M != -INFINITY) {
-      for (int r = 0; r < R; ++r) {
-        const float wt = expf(lse_parts[r * l_sr + row * l_srow] - M);
-        A = fmaf(wt, o_parts[r * o_sr + row * o_srow + d], A);
-      }
-      A /= W;
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((tid & 31) == 0) red[tid >> 5] = mx;
+  __syncthreads();
+  if (tid == 0) s_m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  __syncthreads();
+  const float M = s_m;
+  float ws = 0.f;
+  for (int r = tid; r < R; r += 128) {
+    const float e = (M == -INFINITY) ? 0.f : expf(w[r] - M);
+    w[r] = e;
+    ws += e;
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) ws += __shfl_xor_sync(0xffffffffu, ws, o);
+  __syncthreads();
+  if ((tid & 31) == 0) red[tid >> 5] = ws;
+  __syncthreads();
+  if (tid == 0) s_w = red[0] + red[1] + red[2] + red[3];
+  __syncthreads();
+  const float W = s_w;
+  const float inv = (W > 0.f) ? 1.0f / W : 0.f;
+  for (int d = tid; d < D; d += 128) {
+    const float* src = o_parts + row * o_srow + d;
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    int r = 0;
+    for (; r + 4 <= R; r += 4) {
+      a0 = fmaf(w[r], src[r * o_sr], a0);
+      a1 = fmaf(w[r + 1], src[(r + 1) * o_sr], a1);
+      a2 = fmaf(w[r + 2], src[(r + 2) * o_sr], a2);
+      a3 = fmaf(w[r + 3], src[(r + 3) * o_sr], a3);
     }
+    for (; r < R; ++r) a0 = fmaf(w[r], src[r * o_sr], a0);
+    const float A = ((a0 + a1) + (a2 + a3)) * inv;
     const long long oi = row * D + d;
     if (out_kind == 0) {
       static_cast<__half*>(out)[oi] = __float2half_rn(A);
@@ -445,7 +505,7 @@ __global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ o_
       static_cast<float*>(out)[oi] = A;
     }
   }
-  if (lse_out != nullptr && threadIdx.x == 0) lse_out[row] = (M == -INFINITY) ? M : M + logf(W);
+  if (lse_out != nullptr && tid == 0) lse_out[row] = (W > 0.f) ? M + logf(W) : -INFINITY;
 }
 
 }  // namespace du

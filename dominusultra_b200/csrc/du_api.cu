@@ -7,6 +7,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <set>
@@ -205,7 +206,7 @@ struct DecodePlan {
 
 // Work items are (unit, split); a persistent grid of resident CTAs walks them round-robin.
 // Units are (b, kv head, group chunk of GT query heads). When units alone cannot give each
-// resident CTA slot (three per SM) several items, each cache is split into contiguous ranges of
+// resident CTA slot (three per SM) two items, each cache is split into contiguous ranges of
 // a whole number of the kernel's chunks (at least four chunks per split), so the per-CTA item
 // counts differ by at most one item of a few chunks.
 DecodePlan plan_decode(int B, int Hq, int Hkv, int L, int D) {
@@ -217,9 +218,14 @@ DecodePlan plan_decode(int B, int Hq, int Hkv, int L, int D) {
   const long long slots = static_cast<long long>(sm_count()) * 3;
   const int chunk = 4096 / D;  // DecodeShape<D>::CK
   const long long min_keys = 4LL * chunk;
+  static const long long per_slot = [] {
+    const char* e = std::getenv("DU_DECODE_ITEMS_PER_SLOT");  // tuning override
+    const long long v = e ? std::atoll(e) : 0;
+    return v > 0 ? v : 2LL;
+  }();
   long long ns = 1;
-  if (units < 8 * slots) {
-    ns = (8 * slots + units - 1) / units;
+  if (units < per_slot * slots) {
+    ns = (per_slot * slots + units - 1) / units;
     const long long max_split = (L + min_keys - 1) / min_keys;
     if (ns > max_split) ns = max_split;
     if (ns < 1) ns = 1;
@@ -290,8 +296,8 @@ int launch_decode_split_d(const du::DecodeParams& prm, int GT, int D, int B, cud
 int launch_merge(const float* o_parts, const float* lse_parts, int R, int rows, int D,
                  long long o_sr, long long o_srow, long long l_sr, long long l_srow, void* out,
                  int out_kind, float* lse_out, cudaStream_t st) {
-  const int threads = D >= 256 ? 256 : (D >= 128 ? 128 : 64);
-  du::merge_kernel<<<rows, threads, 0, st>>>(o_parts, lse_parts, R, D, o_sr, o_srow, l_sr, l_srow,
+  if (R > du::MERGE_MAX_R) return fail(DU_ERR_UNSUPPORTED, "more partials than the merge supports");
+  du::merge_kernel<<<rows, 128, 0, st>>>(o_parts, lse_parts, R, D, o_sr, o_srow, l_sr, l_srow,
                                              out, out_kind, lse_out);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "merge launch");

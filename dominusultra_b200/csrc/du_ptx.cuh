@@ -357,6 +357,11 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
   return r;
 }
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
 __device__ __forceinline__ float max3(float a, float b, float c) {
   float r;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
@@ -402,6 +407,43 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
   } else {
     __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
+  }
+}
+
+// Widen a packed pair of 16-bit values to an fp32 pair.
+template <bool BF16>
+__device__ __forceinline__ uint64_t widen2(uint32_t w) {
+  if constexpr (BF16) {
+    return f2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+  } else {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w));
+    return f2(f.x, f.y);
+  }
+}
+
+// Half-split rotation of two element pairs at once in the input dtype:
+// r1 = x1 * c - x2 * s, r2 = x2 * c + x1 * s (packed bf16x2 / f16x2 arithmetic).
+template <bool BF16>
+__device__ __forceinline__ void rope_rotate2(uint32_t x1, uint32_t x2, uint32_t c, uint32_t s,
+                                             uint32_t& r1, uint32_t& r2) {
+  if constexpr (BF16) {
+    const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&x1);
+    const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&x2);
+    const __nv_bfloat162 cc = *reinterpret_cast<const __nv_bfloat162*>(&c);
+    const __nv_bfloat162 ss = *reinterpret_cast<const __nv_bfloat162*>(&s);
+    const __nv_bfloat162 y1 = __hfma2(a, cc, __hneg2(__hmul2(b, ss)));
+    const __nv_bfloat162 y2 = __hfma2(b, cc, __hmul2(a, ss));
+    r1 = *reinterpret_cast<const uint32_t*>(&y1);
+    r2 = *reinterpret_cast<const uint32_t*>(&y2);
+  } else {
+    const __half2 a = *reinterpret_cast<const __half2*>(&x1);
+    const __half2 b = *reinterpret_cast<const __half2*>(&x2);
+    const __half2 cc = *reinterpret_cast<const __half2*>(&c);
+    const __half2 ss = *reinterpret_cast<const __half2*>(&s);
+    const __half2 y1 = __hfma2(a, cc, __hneg2(__hmul2(b, ss)));
+    const __half2 y2 = __hfma2(b, cc, __hmul2(a, ss));
+    r1 = *reinterpret_cast<const uint32_t*>(&y1);
+    r2 = *reinterpret_cast<const uint32_t*>(&y2);
   }
 }
 
