@@ -37,7 +37,12 @@ _sz = ctypes.c_size_t
 SIGNATURES = {
     "du_version": (_i, []),
     "du_last_error": (ctypes.c_char_p, []),
-    "du_prefill": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _ll, _vp]),
+    "du_prefill_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
+    "du_prefill": (
+        _i,
+        [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _ll, _vp, _sz, _vp],
+    ),
+    "du_rope": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _ll, _ll, _i, _vp]),
     "du_decode_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
     "du_decode": (
         _i,

@@ -202,25 +202,35 @@ def dominus_ultra_prefill(
     lse = torch.empty((B, Hq, T), dtype=torch.float32, device=q.device)
     scale = 1.0 / (D**0.5)
     with _OnDevice(q.device):
+        stream = _stream(q.device)
+        ws, ws_bytes = _cached_workspace(
+            "prefill", int(lib.du_prefill_workspace_size(B, Hq, KvH, T, D)), q.device, stream
+        )
         rc = lib.du_prefill(
             _ptr(q), _ptr(k), _ptr(v), _ptr(cos), _ptr(sin), _ptr(out), _ptr(lse),
             B, Hq, KvH, T, D, _dtype_code(q.dtype), scale,
-            min(cos.shape[0], sin.shape[0]), _stream(q.device),
+            min(cos.shape[0], sin.shape[0]), ws, ws_bytes, stream,
         )
     _lib.check(rc, "du_prefill")
     return out, lse
 
 
-def _workspace(B: int, Hq: int, Hkv: int, L: int, D: int, device, stream: int):
-    nbytes = int(_lib.load().du_decode_workspace_size(B, Hq, Hkv, L, D))
+def _cached_workspace(kind: str, nbytes: int, device, stream: int):
+    """(pointer, bytes) of a per-(kind, device, stream) scratch buffer of at least nbytes, grown on
+    demand. Calls on one stream are ordered, so reusing the buffer across them is safe."""
     if nbytes == 0:
         return 0, 0
-    key = (device.index, stream)
+    key = (kind, device.index, stream)
     ws = _WORKSPACES.get(key)
     if ws is None or ws.numel() < nbytes:
         ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
         _WORKSPACES[key] = ws
     return ws.data_ptr(), ws.numel()
+
+
+def _workspace(B: int, Hq: int, Hkv: int, L: int, D: int, device, stream: int):
+    nbytes = int(_lib.load().du_decode_workspace_size(B, Hq, Hkv, L, D))
+    return _cached_workspace("decode", nbytes, device, stream)
 
 
 def dominus_ultra_decode(

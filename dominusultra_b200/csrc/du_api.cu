@@ -9,6 +9,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <set>
 #include <utility>
@@ -16,8 +17,9 @@
 
 #include "../../include/dominus_ultra_b200.h"
 #include "decode_sm100.cuh"
+#include "prefill_fa_sm100.cuh"
 #include "prefill_sm100.cuh"
-#include "prefill_pair_sm100.cuh"
+#include "rope_sm100.cuh"
 
 namespace du {
 
@@ -146,35 +148,91 @@ cudaError_t ensure_smem_attr(Kern kern, int bytes) {
   return e;
 }
 
+// Launch the standalone rotary kernel over rows = B * H * T rows of D elements.
+template <bool BF16, bool OUT_F16, bool BACKWARD>
+int launch_rope_t(const du::RopeParams& rp, cudaStream_t st) {
+  const long long total = rp.rows * (rp.D / 16);
+  long long blocks = (total + 255) / 256;
+  const long long cap = static_cast<long long>(sm_count()) * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  du::rope_kernel<BF16, OUT_F16, BACKWARD><<<static_cast<unsigned>(blocks), 256, 0, st>>>(rp);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "rope launch");
+  return DU_OK;
+}
+
+int launch_rope(const du::RopeParams& rp, bool bf16, bool out_f16, bool backward, cudaStream_t st) {
+  if (bf16) {
+    if (out_f16) return backward ? launch_rope_t<true, true, true>(rp, st) : launch_rope_t<true, true, false>(rp, st);
+    return backward ? launch_rope_t<true, false, true>(rp, st) : launch_rope_t<true, false, false>(rp, st);
+  }
+  return backward ? launch_rope_t<false, false, true>(rp, st) : launch_rope_t<false, false, false>(rp, st);
+}
+
+// Registers per thread the kernel was built with, once per kernel: a setmaxnreg split that asks
+// for more registers than the launch provides would never complete, so launches check it.
+template <typename Kern>
+int launch_registers(Kern kern) {
+  static std::mutex mu;
+  static std::map<const void*, int> regs;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = regs.find(reinterpret_cast<const void*>(kern));
+  if (it != regs.end()) return it->second;
+  cudaFuncAttributes attr{};
+  if (cudaFuncGetAttributes(&attr, kern) != cudaSuccess) return -1;
+  regs[reinterpret_cast<const void*>(kern)] = attr.numRegs;
+  return attr.numRegs;
+}
+
+// Bytes of the rotated-key buffer du_prefill needs (fp16 R(K), [B, Hkv, T, D]).
+size_t prefill_ws_bytes(int B, int Hkv, int T, int D) {
+  if (D > 128) return 0;
+  return static_cast<size_t>(B) * Hkv * T * D * 2;
+}
+
 template <int D, bool BF16>
 int launch_prefill_t(const void* q, const void* k, const void* v, du::PrefillParams prm, int B,
-                     long long rope_positions, cudaStream_t st) {
+                     long long rope_positions, void* ws, cudaStream_t st) {
   const int dtype = BF16 ? DU_DTYPE_BF16 : DU_DTYPE_F16;
   CUtensorMap tq, tk, tv;
   int rc;
   cudaError_t e;
   if constexpr (D <= 128) {
-    // Two query tiles per CTA.
-    using S = du::PairShape<D>;
-    CUtensorMap tc, ts;
+    // 1) R(K) once per (b, kv head), fp16, into the workspace.
+    du::RopeParams rp{};
+    rp.x = k;
+    rp.cos = prm.cos;
+    rp.sin = prm.sin;
+    rp.out = ws;
+    rp.rows = static_cast<long long>(B) * prm.Hkv * prm.T;
+    rp.T = prm.T;
+    rp.D = D;
+    rp.pos_offset = 0;
+    if ((rc = launch_rope(rp, BF16, true, false, st)) != DU_OK) return rc;
+    // 2) attention over two query tiles per CTA.
+    using S = du::FaShape<D>;
     if ((rc = encode_map(&tq, q, dtype, D, prm.T, static_cast<long long>(B) * prm.Hq, S::SPAN / 2,
                          S::BM, S::SPAN)) != DU_OK)
       return rc;
-    if ((rc = encode_map(&tk, k, dtype, D, prm.T, static_cast<long long>(B) * prm.Hkv,
+    if ((rc = encode_map(&tk, ws, DU_DTYPE_F16, D, prm.T, static_cast<long long>(B) * prm.Hkv,
                          S::SPAN / 2, S::BN, S::SPAN)) != DU_OK)
       return rc;
     if ((rc = encode_map(&tv, v, dtype, D, prm.T, static_cast<long long>(B) * prm.Hkv,
                          S::SPAN / 2, S::BN, S::SPAN)) != DU_OK)
       return rc;
-    if ((rc = encode_map_2d(&tc, prm.cos, dtype, D / 2, rope_positions, S::BN)) != DU_OK) return rc;
-    if ((rc = encode_map_2d(&ts, prm.sin, dtype, D / 2, rope_positions, S::BN)) != DU_OK) return rc;
     prm.n_qtiles = (prm.T + 2 * S::BM - 1) / (2 * S::BM);  // query-tile pairs
-    auto kern = du::prefill_pair_kernel<D, BF16>;
+    auto kern = du::prefill_fa_kernel<D, BF16>;
+    const int regs = launch_registers(kern);
+    if (regs * S::NTHREADS < 2 * 128 * S::REG_SOFTMAX + 128 * S::REG_OTHER)
+      return fail(DU_ERR_CUDA, "prefill kernel built with too few registers for its split");
     e = ensure_smem_attr(kern, S::SMEM_BYTES);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(prefill)");
     dim3 grid(static_cast<unsigned>(B * prm.Hq), static_cast<unsigned>(prm.n_qtiles));
-    kern<<<grid, S::NTHREADS, S::SMEM_BYTES, st>>>(tq, tk, tv, tc, ts, prm);
+    kern<<<grid, S::NTHREADS, S::SMEM_BYTES, st>>>(tq, tk, tv, prm);
   } else {
+    (void)rope_positions;
+    (void)ws;
     using S = du::PrefillShape<D>;
     if ((rc = encode_map(&tq, q, dtype, D, prm.T, static_cast<long long>(B) * prm.Hq, S::SPAN / 2,
                          S::BM, S::SPAN)) != DU_OK)
@@ -392,9 +450,15 @@ int du_version(void) { return 100; }
 
 const char* du_last_error(void) { return g_last_error.c_str(); }
 
+size_t du_prefill_workspace_size(int B, int Hq, int Hkv, int T, int D) {
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || T <= 0 || Hq % Hkv != 0 || !valid_head_dim(D)) return 0;
+  return prefill_ws_bytes(B, Hkv, T, D);
+}
+
 int du_prefill(const void* q, const void* k, const void* v, const void* cos, const void* sin,
                void* out, float* lse, int B, int Hq, int Hkv, int T, int D, int dtype,
-               float scale, long long rope_positions, void* stream) {
+               float scale, long long rope_positions, void* workspace, size_t workspace_bytes,
+               void* stream) {
   g_last_error.clear();
   int rc = check_common(B, Hq, Hkv, T, D, dtype);
   if (rc != DU_OK) return rc;
@@ -406,6 +470,10 @@ int du_prefill(const void* q, const void* k, const void* v, const void* cos, con
   if (rope_positions < T) return fail(DU_ERR_INVALID, "rope tables have fewer than T positions");
   if (!(scale > 0.f)) return fail(DU_ERR_INVALID, "scale must be positive");
   if ((T + 127) / 128 > 65535) return fail(DU_ERR_UNSUPPORTED, "sequence length too large");
+  const size_t need = prefill_ws_bytes(B, Hkv, T, D);
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned16(workspace)))
+    return fail(DU_ERR_WORKSPACE, "prefill workspace of " + std::to_string(need) +
+                                      " bytes (16-byte aligned) is required");
   du::PrefillParams prm{};
   prm.cos = cos;
   prm.sin = sin;
@@ -418,19 +486,49 @@ int du_prefill(const void* q, const void* k, const void* v, const void* cos, con
   prm.scale_log2 = scale * 1.4426950408889634f;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool bf16 = dtype == DU_DTYPE_BF16;
+  void* ws = workspace;
   switch (D) {
-    case 16: return bf16 ? launch_prefill_t<16, true>(q, k, v, prm, B, rope_positions, st)
-                         : launch_prefill_t<16, false>(q, k, v, prm, B, rope_positions, st);
-    case 32: return bf16 ? launch_prefill_t<32, true>(q, k, v, prm, B, rope_positions, st)
-                         : launch_prefill_t<32, false>(q, k, v, prm, B, rope_positions, st);
-    case 64: return bf16 ? launch_prefill_t<64, true>(q, k, v, prm, B, rope_positions, st)
-                         : launch_prefill_t<64, false>(q, k, v, prm, B, rope_positions, st);
-    case 128: return bf16 ? launch_prefill_t<128, true>(q, k, v, prm, B, rope_positions, st)
-                          : launch_prefill_t<128, false>(q, k, v, prm, B, rope_positions, st);
-    case 256: return bf16 ? launch_prefill_t<256, true>(q, k, v, prm, B, rope_positions, st)
-                          : launch_prefill_t<256, false>(q, k, v, prm, B, rope_positions, st);
+    case 16: return bf16 ? launch_prefill_t<16, true>(q, k, v, prm, B, rope_positions, ws, st)
+                         : launch_prefill_t<16, false>(q, k, v, prm, B, rope_positions, ws, st);
+    case 32: return bf16 ? launch_prefill_t<32, true>(q, k, v, prm, B, rope_positions, ws, st)
+                         : launch_prefill_t<32, false>(q, k, v, prm, B, rope_positions, ws, st);
+    case 64: return bf16 ? launch_prefill_t<64, true>(q, k, v, prm, B, rope_positions, ws, st)
+                         : launch_prefill_t<64, false>(q, k, v, prm, B, rope_positions, ws, st);
+    case 128: return bf16 ? launch_prefill_t<128, true>(q, k, v, prm, B, rope_positions, ws, st)
+                          : launch_prefill_t<128, false>(q, k, v, prm, B, rope_positions, ws, st);
+    case 256: return bf16 ? launch_prefill_t<256, true>(q, k, v, prm, B, rope_positions, ws, st)
+                          : launch_prefill_t<256, false>(q, k, v, prm, B, rope_positions, ws, st);
     default: return fail(DU_ERR_UNSUPPORTED, "head_dim must be one of 16, 32, 64, 128, 256");
   }
+}
+
+int du_rope(const void* x, const void* cos, const void* sin, void* out, int B, int H, int T, int D,
+            int dtype, int out_dtype, long long pos_offset, long long rope_positions, int backward,
+            void* stream) {
+  g_last_error.clear();
+  if (B <= 0 || H <= 0 || T <= 0) return fail(DU_ERR_INVALID, "batch, heads, and sequence length must be positive");
+  if (!valid_head_dim(D))
+    return fail(DU_ERR_UNSUPPORTED, "head_dim must be a power of two between 16 and 256");
+  if (dtype != DU_DTYPE_F16 && dtype != DU_DTYPE_BF16)
+    return fail(DU_ERR_INVALID, "dtype must be DU_DTYPE_F16 or DU_DTYPE_BF16");
+  if (out_dtype != dtype && out_dtype != DU_DTYPE_F16)
+    return fail(DU_ERR_INVALID, "out_dtype must be the input dtype or DU_DTYPE_F16");
+  if (!x || !cos || !sin || !out) return fail(DU_ERR_INVALID, "null pointer argument");
+  if (!aligned16(x) || !aligned16(cos) || !aligned16(sin) || !aligned16(out))
+    return fail(DU_ERR_INVALID, "all tensors must be 16-byte aligned");
+  if (pos_offset < 0 || pos_offset + T > rope_positions)
+    return fail(DU_ERR_INVALID, "rope tables do not cover the positions");
+  du::RopeParams rp{};
+  rp.x = x;
+  rp.cos = cos;
+  rp.sin = sin;
+  rp.out = out;
+  rp.rows = static_cast<long long>(B) * H * T;
+  rp.T = T;
+  rp.D = D;
+  rp.pos_offset = pos_offset;
+  return launch_rope(rp, dtype == DU_DTYPE_BF16, out_dtype == DU_DTYPE_F16 && dtype != DU_DTYPE_F16,
+                     backward != 0, static_cast<cudaStream_t>(stream));
 }
 
 size_t du_decode_workspace_size(int B, int Hq, int Hkv, int L, int D) {

@@ -89,6 +89,12 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parit
   return ok != 0;
 }
 
+// Suspend-time hint of the slow path of mbar_wait (0: plain try_wait, which the hardware may
+// still suspend for a short system-defined time).
+#ifndef DU_WAIT_SLEEP_NS
+#define DU_WAIT_SLEEP_NS 20000u
+#endif
+
 // Bounded parity wait. `failed` is a per-CTA shared flag: once any thread of the CTA has timed
 // out, every later slow wait gives up at once, so the whole CTA drains quickly.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* failed,
@@ -97,8 +103,46 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   const uint64_t t0 = globaltimer();
   uint32_t n = 0;
   while (true) {
-    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+#if DU_WAIT_SLEEP_NS > 0
+    if (mbar_try_wait_sleep(bar, parity, DU_WAIT_SLEEP_NS)) return true;
+#else
+    if (mbar_try_wait(bar, parity)) return true;
+#endif
     if ((++n & 63u) == 0u) {
+      if (*failed) return false;
+      if (globaltimer() - t0 > DU_WAIT_TIMEOUT_NS) {
+        record_timeout(site);
+        *failed = 1;
+        return false;
+      }
+    }
+  }
+}
+
+// Non-blocking phase test: never suspends the thread.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded parity wait that polls without suspending, for single-thread MMA issuers: a
+// suspended waiter can take a thousand cycles or more to resume on an SM whose other warps
+// keep the issue slots busy, and every such delay lands on the tensor-core critical path.
+__device__ __forceinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity, volatile int* failed,
+                                               unsigned int site) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  uint32_t n = 0;
+  while (true) {
+    if (mbar_test_wait(bar, parity)) return true;
+    if ((++n & 255u) == 0u) {
       if (*failed) return false;
       if (globaltimer() - t0 > DU_WAIT_TIMEOUT_NS) {
         record_timeout(site);
@@ -190,6 +234,18 @@ __device__ __forceinline__ void tc_fence_before() {
 
 __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// True in exactly one lane of the (converged) warp: the lane that issues single-thread
+// tcgen05 operations while the whole warp walks the schedule.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(pred));
+  return pred != 0;
 }
 
 // D[tmem] (+)= A[smem] * B[smem], kind::f16 (fp16/bf16 operands, fp32 accumulate), one CTA.

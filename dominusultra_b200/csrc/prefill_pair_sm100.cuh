@@ -41,6 +41,11 @@
 #include "du_ptx.cuh"
 #include "prefill_sm100.cuh"
 
+// Which of every 8 score pairs take the FMA-pipe exponential (bit i: pair i of 8).
+#ifndef DU_POLY_MASK
+#define DU_POLY_MASK 0x49
+#endif
+
 namespace du {
 
 template <int D>
@@ -104,14 +109,13 @@ __global__ void __launch_bounds__(512, 1)
   const int kvh = h / (p.Hq / p.Hkv);
   const int kv_row = b * p.Hkv + kvh;
   const int T = p.T;
-  const int q0[2] = {pair * 2 * BM, pair * 2 * BM + BM};
-  int n_kv[2];
-#pragma unroll
-  for (int x = 0; x < 2; ++x) {
-    const int q_end = min(q0[x] + BM, T);
-    n_kv[x] = (q0[x] < T) ? (q_end - 1) / BN + 1 : 0;
-  }
-  const int n_kv_all = max(n_kv[0], n_kv[1]);
+  // Scalars, not arrays: a runtime-indexed local array would live in local memory.
+  const int q0a = pair * 2 * BM, q0b = q0a + BM;
+  const int nkva = (q0a < T) ? (min(q0a + BM, T) - 1) / BN + 1 : 0;
+  const int nkvb = (q0b < T) ? (min(q0b + BM, T) - 1) / BN + 1 : 0;
+  auto q0 = [&](int x) { return x ? q0b : q0a; };
+  auto n_kv = [&](int x) { return x ? nkvb : nkva; };
+  const int n_kv_all = max(nkva, nkvb);
 
   auto bar = [&](int i) -> uint32_t { return sbase + S::OFF_BAR + 8u * static_cast<uint32_t>(i); };
   const uint32_t BAR_QF = bar(0);
@@ -166,8 +170,8 @@ __global__ void __launch_bounds__(512, 1)
     regs_inc<S::REG_SOFTMAX>();
     const int x = warp >> 2;           // which query tile
     const int row = tid - 128 * x;     // row within the tile = TMEM lane
-    const int qrow = q0[x] + row;
-    const int nk = n_kv[x];
+    const int qrow = q0(x) + row;
+    const int nk = n_kv(x);
     const uint32_t q_tile = sbase + (x ? S::OFF_QB : S::OFF_QA);
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t s_addr = tmem + lane_off + S::TM_S + x * BN;
@@ -217,7 +221,7 @@ __global__ void __launch_bounds__(512, 1)
       tc_fence_before();
       mbar_arrive(BAR_SR(x));  // S is in registers: the next Q K^T may overwrite it
       const int k0 = j * BN;
-      const bool diag = k0 + BN - 1 > q0[x];  // tile crosses this query tile's diagonal
+      const bool diag = k0 + BN - 1 > q0(x);  // tile crosses this query tile's diagonal
       if (diag) {
 #pragma unroll
         for (int c = 0; c < BN; ++c)
@@ -242,7 +246,7 @@ __global__ void __launch_bounds__(512, 1)
         const float2 xx = f2_split(f2_fma(f2(s[c], s[c + 1]), SL2, NM));
         float2 pp;
         const int q8 = (c / 2) % 8;
-        if (q8 == 0 || q8 == 3 || q8 == 6) {
+        if ((DU_POLY_MASK >> q8) & 1) {
           pp = ex2_poly2(xx.x, xx.y);
         } else {
           pp = make_float2(ex2(xx.x), ex2(xx.y));
@@ -317,13 +321,13 @@ __global__ void __launch_bounds__(512, 1)
       tma_prefetch_desc(&tm_v);
       tma_prefetch_desc(&tm_cos);
       tma_prefetch_desc(&tm_sin);
-      const int n_q = n_kv[1] > 0 ? 2 : 1;  // tile B is skipped when it lies past T
+      const int n_q = nkvb > 0 ? 2 : 1;  // tile B is skipped when it lies past T
       mbar_expect_tx(BAR_QF, n_q * S::Q_BYTES);
       for (int x = 0; x < n_q; ++x)
 #pragma unroll
         for (int blk = 0; blk < S::NBLK; ++blk)
           tma_load_3d(sbase + (x ? S::OFF_QB : S::OFF_QA) + blk * BM * SPAN, &tm_q, BAR_QF,
-                      blk * (SPAN / 2), q0[x], bh);
+                      blk * (SPAN / 2), q0(x), bh);
       int issued_k = 0, issued_v = 0;
       bool ok = true;
       for (int j = 0; ok && j < n_kv_all; ++j) {
@@ -331,7 +335,7 @@ __global__ void __launch_bounds__(512, 1)
         const int jp = j - NS;  // previous use of this stage
         if (jp >= 0) {
           for (int x = 0; x < 2 && ok; ++x)
-            if (jp < n_kv[x]) ok = mbar_wait(BAR_KE(x, s), (jp / NS) & 1, failed, 110);
+            if (jp < n_kv(x)) ok = mbar_wait(BAR_KE(x, s), (jp / NS) & 1, failed, 110);
           if (!ok) break;
         }
         mbar_expect_tx(BAR_KF(s), S::KV_BYTES + 2 * S::CS_BYTES);
@@ -345,7 +349,7 @@ __global__ void __launch_bounds__(512, 1)
         issued_k = j + 1;
         if (jp >= 0) {
           for (int x = 0; x < 2 && ok; ++x)
-            if (jp < n_kv[x]) ok = mbar_wait(BAR_VE(x, s), (jp / NS) & 1, failed, 111);
+            if (jp < n_kv(x)) ok = mbar_wait(BAR_VE(x, s), (jp / NS) & 1, failed, 111);
           if (!ok) break;
         }
         mbar_expect_tx(BAR_VF(s), S::KV_BYTES);
@@ -369,13 +373,13 @@ __global__ void __launch_bounds__(512, 1)
     if (lane == 0) {
       bool ok = true;
       for (int x = 0; x < 2 && ok; ++x)
-        if (n_kv[x] > 0) ok = mbar_wait(BAR_QR(x), 0, failed, 121);
+        if (n_kv(x) > 0) ok = mbar_wait(BAR_QR(x), 0, failed, 121);
       tc_fence_after();
       for (int j = 0; ok && j < n_kv_all; ++j) {
         const int s = j % NS;
         if (!mbar_wait(BAR_KR(s), (j / NS) & 1, failed, 120)) break;
         for (int x = 0; x < 2; ++x) {
-          if (j >= n_kv[x]) continue;
+          if (j >= n_kv(x)) continue;
           // S_x(j-1) must be in the softmax's registers before S_x(j) overwrites it.
           if (j > 0 && !mbar_wait(BAR_SR(x), (j - 1) & 1, failed, 122)) {
             ok = false;
@@ -407,7 +411,7 @@ __global__ void __launch_bounds__(512, 1)
     // ------------------------------------------------------------------ PV issuers A / B
     regs_dec<S::REG_OTHER>();
     const int x = warp - 14;
-    const int nk = n_kv[x];
+    const int nk = n_kv(x);
     if (lane == 0) {
       const uint32_t p_tmem = tmem + S::TM_P + x * (BN / 2);
       const uint32_t o_tmem = tmem + S::TM_O + x * D;

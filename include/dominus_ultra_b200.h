@@ -40,14 +40,36 @@ int du_version(void);
 const char* du_last_error(void);
 
 /*
+ * Workspace bytes du_prefill needs for these sizes: the rotated keys R(K) as fp16
+ * [B, Hkv, T, D] for head_dim <= 128, 0 for head_dim 256.
+ */
+size_t du_prefill_workspace_size(int B, int Hq, int Hkv, int T, int D);
+
+/*
  * Causal fused-RoPE prefill. Replaces the launch of `prefill_kernel` in
  * `dominus_ultra_prefill` (reference dominus_ultra.py:416-501, kernel :119-285).
  * Rows use positions 0..T-1 of the tables; `rope_positions` is the table length (>= T).
  * `scale` is the softmax scale (the reference uses 1/sqrt(D), dominus_ultra.py:475).
+ * For head_dim <= 128 the keys are rotated once per (b, kv head) into `workspace` (see
+ * du_prefill_workspace_size; DU_ERR_WORKSPACE when missing or too small), then the attention
+ * kernel reads them; queries are rotated inside the attention kernel.
  */
 int du_prefill(const void* q, const void* k, const void* v, const void* cos, const void* sin,
                void* out, float* lse, int B, int Hq, int Hkv, int T, int D, int dtype,
-               float scale, long long rope_positions, void* stream);
+               float scale, long long rope_positions, void* workspace, size_t workspace_bytes,
+               void* stream);
+
+/*
+ * Standalone half-split RoPE over x [B, H, T, D] (contiguous): row t rotates at position
+ * pos_offset + t of the tables (pos_offset + T <= rope_positions). backward != 0 applies the
+ * transpose rotation (the gradient of the forward one). Replaces the launch of `_rope_kernel`
+ * in the reference rope.py:19-107 (`apply_rope` / `apply_rope_backward`, :179-220), one tensor
+ * per call. out_dtype is dtype, or DU_DTYPE_F16 for a bf16 input (rotated operands for an
+ * fp16 tensor-core product). out may alias x.
+ */
+int du_rope(const void* x, const void* cos, const void* sin, void* out, int B, int H, int T, int D,
+            int dtype, int out_dtype, long long pos_offset, long long rope_positions, int backward,
+            void* stream);
 
 /*
  * Workspace bytes du_decode / du_decode_partial need for these sizes on the current device

@@ -7,6 +7,7 @@ CPU baseline. The product path (``dominusultra_b200``) never imports it.
 
 from .oracle import (  # noqa: F401
     apply_rope,
+    apply_rope_backward,
     decode,
     decode_partial,
     merge_partials,

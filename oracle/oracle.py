@@ -78,6 +78,19 @@ def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.T
     return torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], dim=-1)
 
 
+def apply_rope_backward(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """Transpose of ``apply_rope`` in fp32 (the BACKWARD branch of the reference ``_rope_kernel``,
+    ``rope.py:62-72``, and its ``_reference(..., backward=True)``, ``rope.py:239-246``):
+    ``x_i c_i + x_{i+D/2} s_i`` and ``x_{i+D/2} c_i - x_i s_i``."""
+    x = x.float()
+    cos = cos.float()
+    sin = sin.float()
+    half = x.shape[-1] // 2
+    x1 = x[..., :half]
+    x2 = x[..., half:]
+    return torch.cat([x1 * cos + x2 * sin, x2 * cos - x1 * sin], dim=-1)
+
+
 def _kv_head(h: int, hq: int, hkv: int) -> int:
     # dominus_ultra.py:168
     return h // (hq // hkv)

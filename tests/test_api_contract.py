@@ -150,19 +150,19 @@ def test_c_abi_rejects_bad_arguments_before_launch():
     null = ctypes.c_void_p(0)
     fake = ctypes.c_void_p(0x10000)
     rc = lib.du_prefill(fake, fake, fake, fake, fake, fake, fake, 0, 8, 8, 128, 64,
-                        _lib.DU_DTYPE_BF16, 0.125, 128, null)
+                        _lib.DU_DTYPE_BF16, 0.125, 128, null, 0, null)
     assert rc == _lib.DU_ERR_INVALID and "positive" in _lib.last_error()
     rc = lib.du_prefill(fake, fake, fake, fake, fake, fake, fake, 1, 8, 3, 128, 64,
-                        _lib.DU_DTYPE_BF16, 0.125, 128, null)
+                        _lib.DU_DTYPE_BF16, 0.125, 128, null, 0, null)
     assert rc == _lib.DU_ERR_INVALID and "divisible" in _lib.last_error()
     rc = lib.du_prefill(fake, fake, fake, fake, fake, fake, fake, 1, 8, 8, 128, 48,
-                        _lib.DU_DTYPE_BF16, 0.125, 128, null)
+                        _lib.DU_DTYPE_BF16, 0.125, 128, null, 0, null)
     assert rc == _lib.DU_ERR_UNSUPPORTED
     rc = lib.du_prefill(fake, fake, fake, fake, fake, fake, fake, 1, 8, 8, 128, 64,
-                        _lib.DU_DTYPE_BF16, 0.125, 127, null)
+                        _lib.DU_DTYPE_BF16, 0.125, 127, null, 0, null)
     assert rc == _lib.DU_ERR_INVALID and "rope" in _lib.last_error()
     rc = lib.du_prefill(ctypes.c_void_p(0x10008), fake, fake, fake, fake, fake, fake, 1, 8, 8,
-                        128, 64, _lib.DU_DTYPE_BF16, 0.125, 128, null)
+                        128, 64, _lib.DU_DTYPE_BF16, 0.125, 128, null, 0, null)
     assert rc == _lib.DU_ERR_INVALID and "aligned" in _lib.last_error()
     rc = lib.du_decode(fake, fake, fake, fake, fake, fake, 1, 8, 8, 128, 64,
                        _lib.DU_DTYPE_F16, 0.125, 128, null, 0, null)

@@ -182,9 +182,10 @@ def test_prefill_guard_bands_untouched(cuda_device):
     lse_buf = torch.full((n_lse + 2 * band,), float("nan"), dtype=torch.float32, device="cuda")
     lib = _lib.load()
     p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    ws = torch.empty(lib.du_prefill_workspace_size(B, Hq, Hkv, T, D), dtype=torch.uint8, device="cuda")
     rc = lib.du_prefill(p(q), p(k), p(v), p(cos), p(sin), ctypes.c_void_p(out_buf[band:].data_ptr()),
                         ctypes.c_void_p(lse_buf[band:].data_ptr()), B, Hq, Hkv, T, D,
-                        _lib.DU_DTYPE_BF16, 1.0 / 8.0, T,
+                        _lib.DU_DTYPE_BF16, 1.0 / 8.0, T, p(ws), ws.numel(),
                         ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     _lib.check(rc, "du_prefill")
     torch.cuda.synchronize()
