@@ -57,21 +57,25 @@ struct DecodeParams {
 
 template <int D, int GT>
 struct DecodeShape {
-  static constexpr int CK = 4096 / D;       // keys per ring stage
-  static constexpr int NSTG = 3;            // 3 stages: three CTAs fit on an SM
+  // Each lane takes PPL half-split chunk pairs (2 x 8 elements each) of a key row; a single
+  // head per unit leaves room in registers for two pairs, which halves the lanes per row.
+  static constexpr int PPL = (GT >= 2 || D < 32) ? 1 : 2;
+  static constexpr int LPR = (D / 16) / PPL;     // lanes per key row
+  static constexpr int KPW = 32 / LPR;           // keys per warp step
+  // Consumer warps: seven for four heads per unit (their ~220 registers allow two warps per
+  // SMSP, one CTA per SM, and the producer is the eighth warp), four otherwise (two or three
+  // CTAs per SM).
+  static constexpr int NW = (GT >= 4) ? 7 : 4;
+  static constexpr int CK_TARGET = 4096 / D;     // ~8 KB of K per stage
+  static constexpr int CK = NW * KPW * ((CK_TARGET / (NW * KPW)) > 1 ? (CK_TARGET / (NW * KPW)) : 1);
+  static constexpr int NSTG = 3;
   static constexpr int ROWB = 2 * D;        // bytes per K / V row
   static constexpr int TABB = D;            // bytes per cos / sin row (D/2 16-bit values)
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = CK * ROWB;
   static constexpr int OFF_C = 2 * CK * ROWB;
   static constexpr int OFF_S = OFF_C + CK * TABB;
-  static constexpr int STAGE = OFF_S + CK * TABB;  // 24 KB
-  // Each lane takes PPL half-split chunk pairs (2 x 8 elements each) of a key row; smaller
-  // groups of heads leave room in registers for two pairs, which halves the lanes per row.
-  static constexpr int PPL = (GT >= 4 || D < 32) ? 1 : 2;
-  static constexpr int LPR = (D / 16) / PPL;     // lanes per key row
-  static constexpr int KPW = 32 / LPR;           // keys per warp step
-  static constexpr int NW = 4;                   // consumer warps
+  static constexpr int STAGE = ((OFF_S + CK * TABB + 127) / 128) * 128;
   static constexpr int STEPS = CK / (NW * KPW);  // steps per warp per chunk
   // Per-item header ring (2 entries): the item's GT query rows, then the cos and sin rows at
   // the query position, copied by the producer like the KV chunks.
@@ -84,12 +88,17 @@ struct DecodeShape {
   static constexpr int OFF_MERGE = OFF_BAR + 8 * (2 * NSTG + 2 + 2 * NHDR) + 16;
   static constexpr int MERGE_BYTES = NW * GT * (D + 2) * 4;
   static constexpr int SMEM_BYTES = OFF_MERGE + MERGE_BYTES + 128;  // + alignment slack
-  static constexpr int NTHREADS = 160;
+  static constexpr int NTHREADS = 32 * (NW + 1);
+  static constexpr int NCONS = 32 * NW;          // consumer threads
   static_assert(STEPS >= 1 && CK % (NW * KPW) == 0, "chunk geometry");
 };
 
 template <int D, bool BF16, int GT>
-__global__ void __launch_bounds__(160, (GT >= 4) ? 1 : 2) decode_kernel(const DecodeParams p) {
+// Resident CTAs per SM: three for one query head per unit (the shared-memory loads of the key
+// rows are the latency to hide, so more warps per SM pay), two for two heads, one for four.
+__global__ void __launch_bounds__(DecodeShape<D, GT>::NTHREADS, (GT == 1) ? 3 : ((GT == 2) ? 2 : 1))
+    decode_kernel(const DecodeParams p) {
+  static_assert(DecodeShape<D, GT>::NTHREADS <= 256 || GT < 4, "two warps per SMSP at most");
   using S = DecodeShape<D, GT>;
   constexpr int LPR = S::LPR, KPW = S::KPW, NSTG = S::NSTG, CK = S::CK, HALF = D / 2;
 
@@ -117,11 +126,11 @@ __global__ void __launch_bounds__(160, (GT >= 4) ? 1 : 2) decode_kernel(const De
       mbar_init(FULL(s), 1);
       mbar_init(EMPTY(s), S::NW);
     }
-    mbar_init(MERGE(0), 128);  // the 128 consumer threads, once per work item
-    mbar_init(MERGE(1), 128);
+    mbar_init(MERGE(0), S::NCONS);  // the consumer threads, once per work item
+    mbar_init(MERGE(1), S::NCONS);
     for (int i = 0; i < S::NHDR; ++i) {
       mbar_init(HFULL(i), 1);
-      mbar_init(HEMPTY(i), 128);
+      mbar_init(HEMPTY(i), S::NCONS);
     }
     *failed = 0;
     mbar_fence_init();
@@ -401,11 +410,11 @@ __global__ void __launch_bounds__(160, (GT >= 4) ? 1 : 2) decode_kernel(const De
         }
       }
     }
-    // Bounded barrier of the four consumer warps (the producer warp keeps streaming).
+    // Bounded barrier of the consumer warps (the producer warp keeps streaming).
     mbar_arrive(MERGE(0));
     ok = mbar_wait(MERGE(0), it & 1, failed, 63);
     if (!__all_sync(0xffffffffu, ok)) break;
-    for (int idx = threadIdx.x; idx < GT * D; idx += 128) {
+    for (int idx = threadIdx.x; idx < GT * D; idx += S::NCONS) {
       const int gg = idx / D;
       const int d = idx - gg * D;
       float M = sm_m[gg];

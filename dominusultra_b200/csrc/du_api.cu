@@ -262,6 +262,26 @@ struct DecodePlan {
   int keys_per_split;
 };
 
+// Keys per ring stage of the decode kernel instantiated for (D, GT): splits are whole chunks.
+template <int D>
+int decode_chunk_d(int GT) {
+  switch (GT) {
+    case 4: return du::DecodeShape<D, 4>::CK;
+    case 2: return du::DecodeShape<D, 2>::CK;
+    default: return du::DecodeShape<D, 1>::CK;
+  }
+}
+
+int decode_chunk(int D, int GT) {
+  switch (D) {
+    case 16: return decode_chunk_d<16>(GT);
+    case 32: return decode_chunk_d<32>(GT);
+    case 64: return decode_chunk_d<64>(GT);
+    case 128: return decode_chunk_d<128>(GT);
+    default: return decode_chunk_d<256>(GT);
+  }
+}
+
 // Work items are (unit, split); a persistent grid of resident CTAs walks them round-robin.
 // Units are (b, kv head, group chunk of GT query heads). When units alone cannot give each
 // resident CTA slot (three per SM) two items, each cache is split into contiguous ranges of
@@ -274,7 +294,7 @@ DecodePlan plan_decode(int B, int Hq, int Hkv, int L, int D) {
   pl.n_gchunk = G / pl.GT;
   const long long units = static_cast<long long>(B) * Hkv * pl.n_gchunk;
   const long long slots = static_cast<long long>(sm_count()) * 3;
-  const int chunk = 4096 / D;  // DecodeShape<D>::CK
+  const int chunk = decode_chunk(D, pl.GT);
   const long long min_keys = 4LL * chunk;
   static const long long per_slot = [] {
     const char* e = std::getenv("DU_DECODE_ITEMS_PER_SLOT");  // tuning override
