@@ -66,16 +66,28 @@ struct DecodeShape {
   // SMSP, one CTA per SM, and the producer is the eighth warp), four otherwise (two or three
   // CTAs per SM).
   static constexpr int NW = (GT >= 4) ? 7 : 4;
+  // K and V stages are TMA tiles of SPAN-byte row blocks with the matching swizzle, the cos and
+  // sin rows tiles of TSPAN-byte blocks; every tile starts on a 1024-byte boundary (swizzled)
+  // or a 128-byte one (16-byte table rows, unswizzled).
+  static constexpr int SPAN = (2 * D >= 128) ? 128 : 2 * D;
+  static constexpr int NBLK = 2 * D / SPAN;
+  static constexpr int TSPAN = (D >= 128) ? 128 : D;
+  static constexpr int TBLK = D / TSPAN;
+  static constexpr int ALIGN_ROWS_K = 1024 / SPAN;
+  static constexpr int ALIGN_ROWS_T = (TSPAN >= 32) ? 1024 / TSPAN : 128 / TSPAN;
+  static constexpr int ALIGN_ROWS = ALIGN_ROWS_K > ALIGN_ROWS_T ? ALIGN_ROWS_K : ALIGN_ROWS_T;
+  static constexpr int CK_BASE = cx_lcm(NW * KPW, ALIGN_ROWS);
   static constexpr int CK_TARGET = 4096 / D;     // ~8 KB of K per stage
-  static constexpr int CK = NW * KPW * ((CK_TARGET / (NW * KPW)) > 1 ? (CK_TARGET / (NW * KPW)) : 1);
-  static constexpr int NSTG = 3;
+  static constexpr int CK = CK_BASE * ((CK_TARGET / CK_BASE) > 1 ? (CK_TARGET / CK_BASE) : 1);
   static constexpr int ROWB = 2 * D;        // bytes per K / V row
   static constexpr int TABB = D;            // bytes per cos / sin row (D/2 16-bit values)
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = CK * ROWB;
   static constexpr int OFF_C = 2 * CK * ROWB;
   static constexpr int OFF_S = OFF_C + CK * TABB;
-  static constexpr int STAGE = ((OFF_S + CK * TABB + 127) / 128) * 128;
+  static constexpr int STAGE = ((OFF_S + CK * TABB + 1023) / 1024) * 1024;
+  static constexpr int STAGE_TX = 2 * CK * ROWB + 2 * CK * TABB;  // bytes landing per stage
+  static constexpr int NSTG = (3 * STAGE <= 200 * 1024) ? 3 : 2;
   static constexpr int STEPS = CK / (NW * KPW);  // steps per warp per chunk
   // Per-item header ring (2 entries): the item's GT query rows, then the cos and sin rows at
   // the query position, copied by the producer like the KV chunks.
@@ -87,24 +99,48 @@ struct DecodeShape {
                                                         // hfull[NHDR], hempty[NHDR], flag
   static constexpr int OFF_MERGE = OFF_BAR + 8 * (2 * NSTG + 2 + 2 * NHDR) + 16;
   static constexpr int MERGE_BYTES = NW * GT * (D + 2) * 4;
-  static constexpr int SMEM_BYTES = OFF_MERGE + MERGE_BYTES + 128;  // + alignment slack
+  static constexpr int SMEM_BYTES = OFF_MERGE + MERGE_BYTES + 1024;  // + alignment slack
   static constexpr int NTHREADS = 32 * (NW + 1);
   static constexpr int NCONS = 32 * NW;          // consumer threads
-  static_assert(STEPS >= 1 && CK % (NW * KPW) == 0, "chunk geometry");
+  // Lane layout: (key slot, lane sub-index) chosen so that the 8 lanes of every quarter-warp
+  // read 16-byte chunks of swizzled rows in 8 distinct bank groups. SUBMASK: lane bits that
+  // differ between the lanes of one key row; KEYMASK: bits that differ between key slots.
+  static constexpr int SUBMASK = (LPR <= 4) ? ((LPR - 1) << 3) : ((LPR == 8) ? 28 : 30);
+  static constexpr int KEYMASK = 31 & ~SUBMASK;
+  static_assert(STEPS >= 1 && CK % (NW * KPW) == 0 && CK <= 256, "chunk geometry");
+  static_assert(CK % ALIGN_ROWS == 0, "tile alignment");
+  static_assert((CK / NW) % (KPW < 8 ? KPW : 8) == 0, "key groups start on swizzle rows");
 };
+
+// (key slot, sub-index) of a consumer lane for LPR lanes per key row (see SUBMASK).
+template <int LPR>
+__device__ __forceinline__ void decode_lane_map(int lane, int& kg, int& sub) {
+  if constexpr (LPR <= 4) {
+    kg = (lane / (8 * LPR)) * 8 + (lane % 8);
+    sub = (lane / 8) % LPR;
+  } else if constexpr (LPR == 8) {
+    kg = lane % 4;
+    sub = (lane / 8) + 4 * ((lane / 4) % 2);
+  } else {
+    kg = lane % 2;
+    sub = ((lane / 8) % 2) + 2 * ((lane / 2) % 4) + 8 * (lane / 16);
+  }
+}
 
 template <int D, bool BF16, int GT>
 // Resident CTAs per SM: three for one query head per unit (the shared-memory loads of the key
 // rows are the latency to hide, so more warps per SM pay), two for two heads, one for four.
 __global__ void __launch_bounds__(DecodeShape<D, GT>::NTHREADS, (GT == 1) ? 3 : ((GT == 2) ? 2 : 1))
-    decode_kernel(const DecodeParams p) {
+    decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                  const __grid_constant__ CUtensorMap tm_cos, const __grid_constant__ CUtensorMap tm_sin,
+                  const DecodeParams p) {
   static_assert(DecodeShape<D, GT>::NTHREADS <= 256 || GT < 4, "two warps per SMSP at most");
   using S = DecodeShape<D, GT>;
   constexpr int LPR = S::LPR, KPW = S::KPW, NSTG = S::NSTG, CK = S::CK, HALF = D / 2;
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_u32 = smem_u32(smem_raw);
-  const uint32_t sbase = (raw_u32 + 127u) & ~127u;
+  const uint32_t sbase = (raw_u32 + 1023u) & ~1023u;
   uint8_t* sgen = smem_raw + (sbase - raw_u32);
   auto FULL = [&](int s) { return sbase + S::OFF_BAR + 8u * static_cast<uint32_t>(s); };
   auto EMPTY = [&](int s) { return sbase + S::OFF_BAR + 8u * static_cast<uint32_t>(NSTG + s); };
@@ -138,14 +174,16 @@ __global__ void __launch_bounds__(DecodeShape<D, GT>::NTHREADS, (GT == 1) ? 3 : 
   }
   __syncthreads();
 
-  const uint8_t* kbase = static_cast<const uint8_t*>(p.k);
-  const uint8_t* vbase = static_cast<const uint8_t*>(p.v);
   const uint8_t* cosb = static_cast<const uint8_t*>(p.cos);
   const uint8_t* sinb = static_cast<const uint8_t*>(p.sin);
 
   if (warp == S::NW) {
     // ------------------------------------------------------------------ bulk-copy producer
     if (lane == 0) {
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      tma_prefetch_desc(&tm_cos);
+      tma_prefetch_desc(&tm_sin);
       int g = 0;  // chunk counter across items (ring stage / phase)
       bool ok = true;
       int it = 0;
@@ -179,15 +217,21 @@ __global__ void __launch_bounds__(DecodeShape<D, GT>::NTHREADS, (GT == 1) ? 3 : 
             ok = false;
             break;
           }
-          const int n = min(CK, kend - c0);
-          const size_t row0 = static_cast<size_t>(bk) * p.L + c0;
-          const size_t tab0 = static_cast<size_t>(p.kv_pos_offset + c0);
+          // Whole boxes always land (rows past the cache or the tables are zero-filled and
+          // masked by the consumers), so every stage completes the same byte count.
+          const int tpos = static_cast<int>(p.kv_pos_offset + c0);
           const uint32_t st = sbase + s * S::STAGE;
-          mbar_expect_tx(FULL(s), static_cast<uint32_t>(n * (2 * S::ROWB + 2 * S::TABB)));
-          bulk_load(st + S::OFF_K, kbase + row0 * S::ROWB, n * S::ROWB, FULL(s));
-          bulk_load(st + S::OFF_V, vbase + row0 * S::ROWB, n * S::ROWB, FULL(s));
-          bulk_load(st + S::OFF_C, cosb + tab0 * S::TABB, n * S::TABB, FULL(s));
-          bulk_load(st + S::OFF_S, sinb + tab0 * S::TABB, n * S::TABB, FULL(s));
+          mbar_expect_tx(FULL(s), static_cast<uint32_t>(S::STAGE_TX));
+#pragma unroll
+          for (int blk = 0; blk < S::NBLK; ++blk) {
+            tma_load_3d(st + S::OFF_K + blk * CK * S::SPAN, &tm_k, FULL(s), blk * (S::SPAN / 2), c0, bk);
+            tma_load_3d(st + S::OFF_V + blk * CK * S::SPAN, &tm_v, FULL(s), blk * (S::SPAN / 2), c0, bk);
+          }
+#pragma unroll
+          for (int tb = 0; tb < S::TBLK; ++tb) {
+            tma_load_2d(st + S::OFF_C + tb * CK * S::TSPAN, &tm_cos, FULL(s), tb * (S::TSPAN / 2), tpos);
+            tma_load_2d(st + S::OFF_S + tb * CK * S::TSPAN, &tm_sin, FULL(s), tb * (S::TSPAN / 2), tpos);
+          }
         }
       }
       // Drain: the last copies land before the CTA may exit.
@@ -201,8 +245,8 @@ __global__ void __launch_bounds__(DecodeShape<D, GT>::NTHREADS, (GT == 1) ? 3 : 
 
   // -------------------------------------------------------------------- consumers (warps 0..3)
   constexpr int PPL = S::PPL;
-  const int kg = lane / LPR;       // key slot within a warp step
-  const int sub = lane % LPR;      // this lane's chunk pairs: sub * PPL + i, i < PPL
+  int kg, sub;  // key slot within a warp step; this lane's chunk pairs: sub * PPL + i, i < PPL
+  decode_lane_map<LPR>(lane, kg, sub);
   int g = 0;
   bool ok = true;
   int it = 0;  // items processed by this CTA (merge-barrier phase)
@@ -288,14 +332,15 @@ __global__ void __launch_bounds__(DecodeShape<D, GT>::NTHREADS, (GT == 1) ? 3 : 
           uint4 k1 = make_uint4(0, 0, 0, 0), k2 = k1, cv = k1, sv = k1;
           vx[u][i][0] = vx[u][i][1] = k1;
           if (valid) {
-            const uint32_t kr = st + S::OFF_K + key * S::ROWB;
-            const uint32_t vr = st + S::OFF_V + key * S::ROWB;
-            k1 = ld_shared_v4(kr + c * 16);
-            k2 = ld_shared_v4(kr + HALF * 2 + c * 16);
-            vx[u][i][0] = ld_shared_v4(vr + c * 16);
-            vx[u][i][1] = ld_shared_v4(vr + HALF * 2 + c * 16);
-            cv = ld_shared_v4(st + S::OFF_C + key * S::TABB + c * 16);
-            sv = ld_shared_v4(st + S::OFF_S + key * S::TABB + c * 16);
+            const uint32_t o1 = swz_chunk_offset<S::SPAN>(CK, key, c);
+            const uint32_t o2 = swz_chunk_offset<S::SPAN>(CK, key, c + D / 16);
+            const uint32_t ot = swz_chunk_offset<S::TSPAN>(CK, key, c);
+            k1 = ld_shared_v4(st + S::OFF_K + o1);
+            k2 = ld_shared_v4(st + S::OFF_K + o2);
+            vx[u][i][0] = ld_shared_v4(st + S::OFF_V + o1);
+            vx[u][i][1] = ld_shared_v4(st + S::OFF_V + o2);
+            cv = ld_shared_v4(st + S::OFF_C + ot);
+            sv = ld_shared_v4(st + S::OFF_S + ot);
           }
           const uint32_t ka[4] = {k1.x, k1.y, k1.z, k1.w};
           const uint32_t kb[4] = {k2.x, k2.y, k2.z, k2.w};
@@ -318,7 +363,8 @@ __global__ void __launch_bounds__(DecodeShape<D, GT>::NTHREADS, (GT == 1) ? 3 : 
           const float2 dd = f2_split(dot[gg]);
           float d = dd.x + dd.y;
 #pragma unroll
-          for (int o = LPR / 2; o >= 1; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+          for (int o = 1; o < 32; o <<= 1)
+            if (S::SUBMASK & o) d += __shfl_xor_sync(0xffffffffu, d, o);
           sc[u][gg] = valid ? d : -INFINITY;
         }
       }
@@ -366,7 +412,8 @@ __global__ void __launch_bounds__(DecodeShape<D, GT>::NTHREADS, (GT == 1) ? 3 : 
 
     // Merge the KPW key groups of the warp (butterfly over lanes with the same chunk pairs).
 #pragma unroll
-    for (int o = LPR; o < 32; o <<= 1) {
+    for (int o = 1; o < 32; o <<= 1) {
+      if (!(S::KEYMASK & o)) continue;
 #pragma unroll
       for (int gg = 0; gg < GT; ++gg) {
         const float mo = __shfl_xor_sync(0xffffffffu, m[gg], o);

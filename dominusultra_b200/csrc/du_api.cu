@@ -122,6 +122,30 @@ int encode_map_2d(CUtensorMap* map, const void* base, int dtype, int cols, long 
   return DU_OK;
 }
 
+// 2-D map over a [rows, cols] 16-bit table: box {box_cols, box_rows}, swizzle for a box row of
+// span_bytes (16: none), zero fill out of bounds.
+int encode_map_2d_sw(CUtensorMap* map, const void* base, int dtype, int cols, long long rows,
+                     int box_cols, int box_rows, int span_bytes) {
+  auto fn = get_encode_fn();
+  if (fn == nullptr) return fail(DU_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapSwizzle sw = span_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : span_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                : span_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                                   : CU_TENSOR_MAP_SWIZZLE_NONE;
+  const CUtensorMapDataType dt =
+      dtype == DU_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(DU_ERR_CUDA, "cuTensorMapEncodeTiled (table) failed with CUresult " + std::to_string(r));
+  return DU_OK;
+}
+
 int sm_count() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 148;
@@ -324,9 +348,19 @@ size_t decode_ws_bytes(const DecodePlan& pl, int B, int Hq, int D) {
 }
 
 template <int D, bool BF16, int GT>
-int launch_decode_split_t(const du::DecodeParams& prm, int B, cudaStream_t st) {
-  (void)B;
+int launch_decode_split_t(const du::DecodeParams& prm, int B, long long rope_positions,
+                          cudaStream_t st) {
   using S = du::DecodeShape<D, GT>;
+  const int dtype = BF16 ? DU_DTYPE_BF16 : DU_DTYPE_F16;
+  CUtensorMap tk, tv, tc, ts;
+  int rc;
+  const long long units = static_cast<long long>(B) * prm.Hkv;
+  if ((rc = encode_map(&tk, prm.k, dtype, D, prm.L, units, S::SPAN / 2, S::CK, S::SPAN)) != DU_OK) return rc;
+  if ((rc = encode_map(&tv, prm.v, dtype, D, prm.L, units, S::SPAN / 2, S::CK, S::SPAN)) != DU_OK) return rc;
+  if ((rc = encode_map_2d_sw(&tc, prm.cos, dtype, D / 2, rope_positions, S::TSPAN / 2, S::CK, S::TSPAN)) != DU_OK)
+    return rc;
+  if ((rc = encode_map_2d_sw(&ts, prm.sin, dtype, D / 2, rope_positions, S::TSPAN / 2, S::CK, S::TSPAN)) != DU_OK)
+    return rc;
   auto kern = du::decode_kernel<D, BF16, GT>;
   cudaError_t e = ensure_smem_attr(kern, S::SMEM_BYTES);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(decode)");
@@ -344,29 +378,30 @@ int launch_decode_split_t(const du::DecodeParams& prm, int B, cudaStream_t st) {
   }
   long long grid = static_cast<long long>(sm_count()) * per_sm;
   if (grid > prm.n_items) grid = prm.n_items;
-  kern<<<static_cast<unsigned>(grid), S::NTHREADS, S::SMEM_BYTES, st>>>(prm);
+  kern<<<static_cast<unsigned>(grid), S::NTHREADS, S::SMEM_BYTES, st>>>(tk, tv, tc, ts, prm);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "decode launch");
   return DU_OK;
 }
 
 template <int D, bool BF16>
-int launch_decode_split_g(const du::DecodeParams& prm, int GT, int B, cudaStream_t st) {
+int launch_decode_split_g(const du::DecodeParams& prm, int GT, int B, long long rp, cudaStream_t st) {
   switch (GT) {
-    case 4: return launch_decode_split_t<D, BF16, 4>(prm, B, st);
-    case 2: return launch_decode_split_t<D, BF16, 2>(prm, B, st);
-    default: return launch_decode_split_t<D, BF16, 1>(prm, B, st);
+    case 4: return launch_decode_split_t<D, BF16, 4>(prm, B, rp, st);
+    case 2: return launch_decode_split_t<D, BF16, 2>(prm, B, rp, st);
+    default: return launch_decode_split_t<D, BF16, 1>(prm, B, rp, st);
   }
 }
 
 template <bool BF16>
-int launch_decode_split_d(const du::DecodeParams& prm, int GT, int D, int B, cudaStream_t st) {
+int launch_decode_split_d(const du::DecodeParams& prm, int GT, int D, int B, long long rp,
+                          cudaStream_t st) {
   switch (D) {
-    case 16: return launch_decode_split_g<16, BF16>(prm, GT, B, st);
-    case 32: return launch_decode_split_g<32, BF16>(prm, GT, B, st);
-    case 64: return launch_decode_split_g<64, BF16>(prm, GT, B, st);
-    case 128: return launch_decode_split_g<128, BF16>(prm, GT, B, st);
-    case 256: return launch_decode_split_g<256, BF16>(prm, GT, B, st);
+    case 16: return launch_decode_split_g<16, BF16>(prm, GT, B, rp, st);
+    case 32: return launch_decode_split_g<32, BF16>(prm, GT, B, rp, st);
+    case 64: return launch_decode_split_g<64, BF16>(prm, GT, B, rp, st);
+    case 128: return launch_decode_split_g<128, BF16>(prm, GT, B, rp, st);
+    case 256: return launch_decode_split_g<256, BF16>(prm, GT, B, rp, st);
     default: return fail(DU_ERR_UNSUPPORTED, "head_dim must be one of 16, 32, 64, 128, 256");
   }
 }
@@ -437,8 +472,8 @@ int decode_impl(const void* q, const void* kc, const void* vc, const void* cos, 
       prm.o_part = out_f32;
       prm.lse_part = lse_f32;
     }
-    return bf16 ? launch_decode_split_d<true>(prm, pl.GT, D, B, st)
-                : launch_decode_split_d<false>(prm, pl.GT, D, B, st);
+    return bf16 ? launch_decode_split_d<true>(prm, pl.GT, D, B, rope_positions, st)
+                : launch_decode_split_d<false>(prm, pl.GT, D, B, rope_positions, st);
   }
   const size_t need = decode_ws_bytes(pl, B, Hq, D);
   if (ws == nullptr || ws_bytes < need || !aligned16(ws))
@@ -450,8 +485,8 @@ int decode_impl(const void* q, const void* kc, const void* vc, const void* cos, 
   prm.mode = 1;
   prm.o_part = o_part;
   prm.lse_part = l_part;
-  rc = bf16 ? launch_decode_split_d<true>(prm, pl.GT, D, B, st)
-            : launch_decode_split_d<false>(prm, pl.GT, D, B, st);
+  rc = bf16 ? launch_decode_split_d<true>(prm, pl.GT, D, B, rope_positions, st)
+            : launch_decode_split_d<false>(prm, pl.GT, D, B, rope_positions, st);
   if (rc != DU_OK) return rc;
   if (out != nullptr)
     return launch_merge(o_part, l_part, pl.n_split, static_cast<int>(rows), D, D,

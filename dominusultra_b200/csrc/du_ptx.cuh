@@ -360,6 +360,9 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int a_fmt, int b_
 }
 
 // Swizzle-mode code for a row span of `span_bytes` (128, 64 or 32).
+__host__ __device__ constexpr int cx_gcd(int a, int b) { return b == 0 ? a : cx_gcd(b, a % b); }
+__host__ __device__ constexpr int cx_lcm(int a, int b) { return a / cx_gcd(a, b) * b; }
+
 __host__ __device__ constexpr uint32_t swizzle_code(int span_bytes) {
   return span_bytes == 128 ? 2u : (span_bytes == 64 ? 4u : 6u);
 }
