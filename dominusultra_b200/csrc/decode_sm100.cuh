@@ -8,9 +8,10 @@
 // (the cache holds positions 0..L-1, the new token is at L and does not attend to itself).
 //
 // The kernel is HBM-bound, so it is laid out for streaming:
-//  * work items are (unit, split) pairs, where a unit is one (b, kv head, group chunk) serving
-//    GT query heads of the GQA group (so each KV byte is read once) and a split is a
-//    contiguous range of its cache; a persistent grid (resident CTAs only) walks the items;
+//  * a unit is one (b, kv head, group chunk) serving GT query heads of the GQA group (so each
+//    KV byte is read once); a persistent grid (resident CTAs only) walks either whole units
+//    round-robin or, when units are fewer than resident CTAs, equal contiguous ranges of the
+//    flattened (unit, chunk) sequence (per-unit fragments with one partial slot each);
 //  * a producer warp streams each item's keys in chunks of CK rows: K, V and the matching
 //    cos/sin table rows are contiguous in memory, so each chunk is four cp.async.bulk copies
 //    (no multicast) into a 3-stage shared-memory ring guarded by mbarriers, and it runs ahead
@@ -23,9 +24,10 @@
 //    fp32 and the dot products / P V sums use packed f32x2 FMAs; scores are reduced across the
 //    lanes of a row with xor-shuffles; the online softmax runs per lane group in the log2
 //    domain and moves its reference max only when a score exceeds it by 2^8;
-//  * at the end of an item the lane groups and warps are merged; with more than one split per
-//    row, each split writes an fp32 partial (out normalised over the split, natural-log LSE)
-//    and merge_kernel combines them.
+//  * at the end of an item the lane groups and warps are merged; when a unit is spread over
+//    several CTAs, each fragment writes an fp32 partial (out normalised over the fragment,
+//    natural-log LSE) into its slot of the row and merge_kernel combines the slots (a merge by
+//    the last fragment through per-unit counters measured slower).
 #pragma once
 
 #include "du_ptx.cuh"
@@ -39,20 +41,74 @@ struct DecodeParams {
   const void* cos;  // [positions, D/2]
   const void* sin;  // [positions, D/2]
   void* out;        // mode 0: [B, Hq, D] in the input dtype
-  float* o_part;    // mode 1: [B * Hq, n_split, D] fp32
-  float* lse_part;  // mode 1: [B * Hq, n_split] fp32
+  float* o_part;    // mode 1: [B * Hq, n_split, D] fp32 (final when n_split == 1)
+  float* lse_part;  // mode 1: [B * Hq, n_split] fp32, natural log
   int Hq;
   int Hkv;
   int L;
   int G;          // Hq / Hkv
   int n_gchunk;   // G / GT
-  int n_split;
-  int keys_per_split;
-  int n_items;    // B * Hkv * n_gchunk * n_split
+  int n_split;    // partial slots per row (1: each unit whole in one CTA, outputs final)
+  int n_units;    // B * Hkv * n_gchunk
+  int cpu;        // chunks per unit = ceil(L / CK)
+  long long total_chunks;  // n_units * cpu
   long long q_pos;
   long long kv_pos_offset;
   float scale_log2;
   int mode;  // 0: final output in dtype (n_split == 1); 1: fp32 partials
+};
+
+// One fragment of a CTA's work: keys [kbeg, kend) of one unit, written to partial slot `slot`.
+struct DecodeFrag {
+  int unit, kbeg, kend, slot;
+  bool last;  // the unit's last fragment
+};
+
+// The CTA's work, walked identically by its producer and consumers. With one slot per row, whole
+// units are dealt round-robin. Otherwise the flattened (unit, chunk) sequence is cut into equal
+// contiguous ranges, one per CTA (per-CTA work differs by at most one chunk, whatever the unit
+// count), and each range into per-unit fragments; a unit's fragments go to consecutive CTAs,
+// the first of them writing slot 0.
+struct DecodeWalk {
+  long long cur, hi;
+  __device__ __forceinline__ void init(const DecodeParams& p) {
+    if (p.n_split == 1) {
+      cur = blockIdx.x;
+      hi = p.n_units;
+    } else {
+      cur = static_cast<long long>(blockIdx.x) * p.total_chunks / gridDim.x;
+      hi = static_cast<long long>(blockIdx.x + 1) * p.total_chunks / gridDim.x;
+    }
+  }
+  // CTA whose range holds global chunk x.
+  __device__ __forceinline__ static int cta_of(const DecodeParams& p, long long x) {
+    const long long G = gridDim.x;
+    long long c = x * G / p.total_chunks;
+    if ((c + 1) * p.total_chunks / G <= x) ++c;
+    return static_cast<int>(c);
+  }
+  __device__ __forceinline__ bool next(const DecodeParams& p, int CK, DecodeFrag& f) {
+    if (cur >= hi) return false;
+    if (p.n_split == 1) {
+      f.unit = static_cast<int>(cur);
+      f.kbeg = 0;
+      f.kend = p.L;
+      f.slot = 0;
+      f.last = true;
+      cur += gridDim.x;
+      return true;
+    }
+    const long long u = cur / p.cpu;
+    const long long ub = u * p.cpu;
+    const long long b = min(hi, ub + p.cpu);
+    f.unit = static_cast<int>(u);
+    f.kbeg = static_cast<int>(cur - ub) * CK;
+    f.kend = min(p.L, static_cast<int>(b - ub) * CK);
+    f.slot = static_cast<int>(blockIdx.x) - cta_of(p, ub);
+    f.last = (b == ub + p.cpu);
+    cur = b;
+    return true;
+  }
 };
 
 template <int D, int GT>
@@ -97,7 +153,8 @@ struct DecodeShape {
   static constexpr int OFF_HDR = NSTG * STAGE;
   static constexpr int OFF_BAR = OFF_HDR + NHDR * HDR;  // full[NSTG], empty[NSTG], merge[2],
                                                         // hfull[NHDR], hempty[NHDR], flag
-  static constexpr int OFF_MERGE = OFF_BAR + 8 * (2 * NSTG + 2 + 2 * NHDR) + 16;
+  static constexpr int N_BAR = 2 * NSTG + 2 + 2 * NHDR;
+  static constexpr int OFF_MERGE = OFF_BAR + 8 * N_BAR + 16;
   static constexpr int MERGE_BYTES = NW * GT * (D + 2) * 4;
   static constexpr int SMEM_BYTES = OFF_MERGE + MERGE_BYTES + 1024;  // + alignment slack
   static constexpr int NTHREADS = 32 * (NW + 1);
@@ -149,8 +206,7 @@ __global__ void __launch_bounds__(DecodeShape<D, GT>::NTHREADS, (GT == 1) ? 3 : 
   auto HEMPTY = [&](int i) {
     return sbase + S::OFF_BAR + 8u * static_cast<uint32_t>(2 * NSTG + 2 + S::NHDR + i);
   };
-  volatile int* failed =
-      reinterpret_cast<volatile int*>(sgen + S::OFF_BAR + 8 * (2 * NSTG + 2 + 2 * S::NHDR));
+  volatile int* failed = reinterpret_cast<volatile int*>(sgen + S::OFF_BAR + 8 * S::N_BAR);
   float* sm_m = reinterpret_cast<float*>(sgen + S::OFF_MERGE);      // [NW][GT]
   float* sm_l = sm_m + S::NW * GT;                                   // [NW][GT]
   float* sm_acc = sm_l + S::NW * GT;                                 // [NW][GT][D]
@@ -187,13 +243,15 @@ __global__ void __launch_bounds__(DecodeShape<D, GT>::NTHREADS, (GT == 1) ? 3 : 
       int g = 0;  // chunk counter across items (ring stage / phase)
       bool ok = true;
       int it = 0;
-      for (int item = blockIdx.x; ok && item < p.n_items; item += gridDim.x, ++it) {
-        const int unit = item / p.n_split;
-        const int split = item - unit * p.n_split;
+      DecodeWalk walk;
+      walk.init(p);
+      DecodeFrag fr;
+      for (; ok && walk.next(p, CK, fr); ++it) {
+        const int unit = fr.unit;
         const int gch = unit % p.n_gchunk;
         const int bk = unit / p.n_gchunk;  // b * Hkv + kvh
-        const int kbeg = split * p.keys_per_split;
-        const int kend = min(p.L, kbeg + p.keys_per_split);
+        const int kbeg = fr.kbeg;
+        const int kend = fr.kend;
         {
           // Item header: query rows of the GT heads and the cos / sin rows at q_pos.
           const int hs = it % S::NHDR;
@@ -250,16 +308,19 @@ __global__ void __launch_bounds__(DecodeShape<D, GT>::NTHREADS, (GT == 1) ? 3 : 
   int g = 0;
   bool ok = true;
   int it = 0;  // items processed by this CTA (merge-barrier phase)
-  for (int item = blockIdx.x; item < p.n_items; item += gridDim.x, ++it) {
-    const int unit = item / p.n_split;
-    const int split = item - unit * p.n_split;
+  DecodeWalk walk;
+  walk.init(p);
+  DecodeFrag fr;
+  for (; walk.next(p, CK, fr); ++it) {
+    const int unit = fr.unit;
+    const int split = fr.slot;
     const int gch = unit % p.n_gchunk;
     const int bk = unit / p.n_gchunk;
     const int b = bk / p.Hkv;
     const int kvh = bk - b * p.Hkv;
     const int h0 = kvh * p.G + gch * GT;
-    const int kbeg = split * p.keys_per_split;
-    const int kend = min(p.L, kbeg + p.keys_per_split);
+    const int kbeg = fr.kbeg;
+    const int kend = fr.kend;
 
     // Rotated, pre-scaled query pairs (log2 domain) for this lane's chunk pairs, from the header.
     uint64_t q1[GT][PPL][4], q2[GT][PPL][4];
@@ -487,6 +548,12 @@ __global__ void __launch_bounds__(DecodeShape<D, GT>::NTHREADS, (GT == 1) ? 3 : 
         if (d == 0)
           p.lse_part[row * p.n_split + split] =
               (Lsum > 0.f) ? (M + lg2(Lsum)) * 0.69314718055994531f : -INFINITY;
+        // The unit's last fragment also marks the row's unused slots empty (weight 0).
+        if (fr.last)
+          for (int sl = split + 1; sl < p.n_split; ++sl) {
+            p.o_part[(row * p.n_split + sl) * D + d] = 0.f;
+            if (d == 0) p.lse_part[row * p.n_split + sl] = -INFINITY;
+          }
       }
     }
     mbar_arrive(MERGE(1));  // merge area free for the next item

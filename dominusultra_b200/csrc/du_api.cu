@@ -282,8 +282,11 @@ int launch_prefill_t(const void* q, const void* k, const void* v, du::PrefillPar
 struct DecodePlan {
   int GT;
   int n_gchunk;
-  int n_split;
-  int keys_per_split;
+  int n_split;   // partial slots per row; 1 = whole units round-robin, final output direct
+  int n_units;
+  int cpu;       // chunks per unit
+  long long total_chunks;
+  int grid;      // CTAs launched (the kernel's resident count per SM x SMs, or fewer)
 };
 
 // Keys per ring stage of the decode kernel instantiated for (D, GT): splits are whole chunks.
@@ -306,36 +309,39 @@ int decode_chunk(int D, int GT) {
   }
 }
 
-// Work items are (unit, split); a persistent grid of resident CTAs walks them round-robin.
-// Units are (b, kv head, group chunk of GT query heads). When units alone cannot give each
-// resident CTA slot (three per SM) two items, each cache is split into contiguous ranges of
-// a whole number of the kernel's chunks (at least four chunks per split), so the per-CTA item
-// counts differ by at most one item of a few chunks.
+// Resident CTAs per SM the decode kernel is built for (its launch bounds): three for one query
+// head per unit, two for two, one for four.
+int decode_residency(int GT) { return GT == 1 ? 3 : (GT == 2 ? 2 : 1); }
+
+// Units are (b, kv head, group chunk of GT query heads). A persistent grid of resident CTAs
+// either takes whole units round-robin (when they divide evenly over the CTAs, or are so many
+// that the last round hardly matters), or cuts the flattened (unit, chunk) sequence into equal
+// contiguous ranges, one per CTA; then a unit is spread over consecutive CTAs, each writing an
+// fp32 partial into its own slot of the row, and merge_kernel combines the slots.
 DecodePlan plan_decode(int B, int Hq, int Hkv, int L, int D) {
   DecodePlan pl{};
   const int G = Hq / Hkv;
   pl.GT = (G % 4 == 0) ? 4 : ((G % 2 == 0) ? 2 : 1);
   pl.n_gchunk = G / pl.GT;
   const long long units = static_cast<long long>(B) * Hkv * pl.n_gchunk;
-  const long long slots = static_cast<long long>(sm_count()) * 3;
+  const long long ctas = static_cast<long long>(sm_count()) * decode_residency(pl.GT);
   const int chunk = decode_chunk(D, pl.GT);
-  const long long min_keys = 4LL * chunk;
-  static const long long per_slot = [] {
-    const char* e = std::getenv("DU_DECODE_ITEMS_PER_SLOT");  // tuning override
-    const long long v = e ? std::atoll(e) : 0;
-    return v > 0 ? v : 2LL;
-  }();
-  long long ns = 1;
-  if (units < per_slot * slots) {
-    ns = (per_slot * slots + units - 1) / units;
-    const long long max_split = (L + min_keys - 1) / min_keys;
-    if (ns > max_split) ns = max_split;
-    if (ns < 1) ns = 1;
+  pl.n_units = static_cast<int>(units);
+  pl.cpu = (L + chunk - 1) / chunk;
+  pl.total_chunks = units * pl.cpu;
+  const long long grid = pl.total_chunks < ctas ? pl.total_chunks : ctas;
+  const long long per = pl.total_chunks / grid;  // chunks per CTA, at least
+  // Whole units when they spread evenly, are plentiful, or are too short to be worth cutting
+  // (fragments of fewer than four chunks would cost more in partials than they balance).
+  if (units % ctas == 0 || units >= 8 * ctas || per < 4) {
+    pl.n_split = 1;
+    pl.grid = static_cast<int>(units < ctas ? units : ctas);
+    return pl;
   }
-  long long kps = (L + ns - 1) / ns;
-  kps = ((kps + chunk - 1) / chunk) * chunk;
-  pl.keys_per_split = static_cast<int>(kps);
-  pl.n_split = static_cast<int>((L + kps - 1) / kps);
+  long long slots = (pl.cpu - 1 + per - 1) / per + 1;  // CTAs one unit's chunks can span
+  if (slots < 2) slots = 2;
+  pl.grid = static_cast<int>(grid);
+  pl.n_split = static_cast<int>(slots);
   return pl;
 }
 
@@ -348,7 +354,7 @@ size_t decode_ws_bytes(const DecodePlan& pl, int B, int Hq, int D) {
 }
 
 template <int D, bool BF16, int GT>
-int launch_decode_split_t(const du::DecodeParams& prm, int B, long long rope_positions,
+int launch_decode_split_t(const du::DecodeParams& prm, int B, long long rope_positions, int grid,
                           cudaStream_t st) {
   using S = du::DecodeShape<D, GT>;
   const int dtype = BF16 ? DU_DTYPE_BF16 : DU_DTYPE_F16;
@@ -364,20 +370,7 @@ int launch_decode_split_t(const du::DecodeParams& prm, int B, long long rope_pos
   auto kern = du::decode_kernel<D, BF16, GT>;
   cudaError_t e = ensure_smem_attr(kern, S::SMEM_BYTES);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(decode)");
-  // Resident CTAs per SM, once per instantiation and device (this function is a distinct
-  // template instance per kernel, so the static table is per kernel).
-  static int per_sm_cache[64] = {};
-  int dev = 0;
-  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-  int per_sm = (dev >= 0 && dev < 64) ? per_sm_cache[dev] : 0;
-  if (per_sm == 0) {
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, S::NTHREADS, S::SMEM_BYTES);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
-    if (per_sm < 1) per_sm = 1;
-    if (dev >= 0 && dev < 64) per_sm_cache[dev] = per_sm;
-  }
-  long long grid = static_cast<long long>(sm_count()) * per_sm;
-  if (grid > prm.n_items) grid = prm.n_items;
+  // The work walk depends on the grid size the plan chose (resident CTAs only).
   kern<<<static_cast<unsigned>(grid), S::NTHREADS, S::SMEM_BYTES, st>>>(tk, tv, tc, ts, prm);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "decode launch");
@@ -385,23 +378,24 @@ int launch_decode_split_t(const du::DecodeParams& prm, int B, long long rope_pos
 }
 
 template <int D, bool BF16>
-int launch_decode_split_g(const du::DecodeParams& prm, int GT, int B, long long rp, cudaStream_t st) {
+int launch_decode_split_g(const du::DecodeParams& prm, int GT, int B, long long rp, int grid,
+                          cudaStream_t st) {
   switch (GT) {
-    case 4: return launch_decode_split_t<D, BF16, 4>(prm, B, rp, st);
-    case 2: return launch_decode_split_t<D, BF16, 2>(prm, B, rp, st);
-    default: return launch_decode_split_t<D, BF16, 1>(prm, B, rp, st);
+    case 4: return launch_decode_split_t<D, BF16, 4>(prm, B, rp, grid, st);
+    case 2: return launch_decode_split_t<D, BF16, 2>(prm, B, rp, grid, st);
+    default: return launch_decode_split_t<D, BF16, 1>(prm, B, rp, grid, st);
   }
 }
 
 template <bool BF16>
 int launch_decode_split_d(const du::DecodeParams& prm, int GT, int D, int B, long long rp,
-                          cudaStream_t st) {
+                          int grid, cudaStream_t st) {
   switch (D) {
-    case 16: return launch_decode_split_g<16, BF16>(prm, GT, B, rp, st);
-    case 32: return launch_decode_split_g<32, BF16>(prm, GT, B, rp, st);
-    case 64: return launch_decode_split_g<64, BF16>(prm, GT, B, rp, st);
-    case 128: return launch_decode_split_g<128, BF16>(prm, GT, B, rp, st);
-    case 256: return launch_decode_split_g<256, BF16>(prm, GT, B, rp, st);
+    case 16: return launch_decode_split_g<16, BF16>(prm, GT, B, rp, grid, st);
+    case 32: return launch_decode_split_g<32, BF16>(prm, GT, B, rp, grid, st);
+    case 64: return launch_decode_split_g<64, BF16>(prm, GT, B, rp, grid, st);
+    case 128: return launch_decode_split_g<128, BF16>(prm, GT, B, rp, grid, st);
+    case 256: return launch_decode_split_g<256, BF16>(prm, GT, B, rp, grid, st);
     default: return fail(DU_ERR_UNSUPPORTED, "head_dim must be one of 16, 32, 64, 128, 256");
   }
 }
@@ -456,8 +450,9 @@ int decode_impl(const void* q, const void* kc, const void* vc, const void* cos, 
   prm.G = Hq / Hkv;
   prm.n_gchunk = pl.n_gchunk;
   prm.n_split = pl.n_split;
-  prm.keys_per_split = pl.keys_per_split;
-  prm.n_items = B * Hkv * pl.n_gchunk * pl.n_split;
+  prm.n_units = pl.n_units;
+  prm.cpu = pl.cpu;
+  prm.total_chunks = pl.total_chunks;
   prm.q_pos = q_pos;
   prm.kv_pos_offset = kv_off;
   prm.scale_log2 = scale * 1.4426950408889634f;
@@ -472,8 +467,8 @@ int decode_impl(const void* q, const void* kc, const void* vc, const void* cos, 
       prm.o_part = out_f32;
       prm.lse_part = lse_f32;
     }
-    return bf16 ? launch_decode_split_d<true>(prm, pl.GT, D, B, rope_positions, st)
-                : launch_decode_split_d<false>(prm, pl.GT, D, B, rope_positions, st);
+    return bf16 ? launch_decode_split_d<true>(prm, pl.GT, D, B, rope_positions, pl.grid, st)
+                : launch_decode_split_d<false>(prm, pl.GT, D, B, rope_positions, pl.grid, st);
   }
   const size_t need = decode_ws_bytes(pl, B, Hq, D);
   if (ws == nullptr || ws_bytes < need || !aligned16(ws))
@@ -485,8 +480,8 @@ int decode_impl(const void* q, const void* kc, const void* vc, const void* cos, 
   prm.mode = 1;
   prm.o_part = o_part;
   prm.lse_part = l_part;
-  rc = bf16 ? launch_decode_split_d<true>(prm, pl.GT, D, B, rope_positions, st)
-            : launch_decode_split_d<false>(prm, pl.GT, D, B, rope_positions, st);
+  rc = bf16 ? launch_decode_split_d<true>(prm, pl.GT, D, B, rope_positions, pl.grid, st)
+            : launch_decode_split_d<false>(prm, pl.GT, D, B, rope_positions, pl.grid, st);
   if (rc != DU_OK) return rc;
   if (out != nullptr)
     return launch_merge(o_part, l_part, pl.n_split, static_cast<int>(rows), D, D,

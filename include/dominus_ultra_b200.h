@@ -73,7 +73,7 @@ int du_rope(const void* x, const void* cos, const void* sin, void* out, int B, i
 
 /*
  * Workspace bytes du_decode / du_decode_partial need for these sizes on the current device
- * (0 when the cache is handled by a single split per row).
+ * (0 when every row's cache is handled by one CTA).
  */
 size_t du_decode_workspace_size(int B, int Hq, int Hkv, int L, int D);
 

@@ -125,7 +125,7 @@ def test_decode_sharded_sequence_merge_matches_full(cuda_device):
 
 
 def test_decode_guard_bands_untouched(cuda_device):
-    B, Hq, Hkv, L, D = 2, 8, 2, 3000, 64
+    B, Hq, Hkv, L, D = 2, 8, 8, 8192, 64
     dtype = torch.bfloat16
     q, k, v, cos, sin = (t.cuda() for t in _inputs(B, Hq, Hkv, L, D, dtype, 5000))
     lib = _lib.load()
