@@ -45,9 +45,10 @@ DECODE = dict(B=8, H=32, Hkv=32, L=2048, D=64, base=10000.0)
 # Long-context Llama-3-8B-shaped decode: the KV sequence is split across the ranks.
 DECODE_LONG = dict(B=4, H=32, Hkv=8, L=131072, D=128, base=500000.0)
 
-# Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) from the ncu captures
-# summarised under profiles/ (None until captured for the current kernel version).
-NCU_TRAFFIC = {"prefill": None, "decode": None}
+# Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum, bytes) of the dominant
+# kernel from the ncu captures summarised under profiles/ (prefill: prefill_fa_kernel at the
+# bench shape; decode: decode_kernel at the bench shape).
+NCU_TRAFFIC = {"prefill": 50655232 + 13824, "decode": 134578176 + 4145920}
 
 
 def prefill_flops(B, H, S, D):
