@@ -134,7 +134,10 @@ __global__ void __launch_bounds__(384, 1)
     tmem_alloc(tmem_slot, S::TMEM_COLS);
     tmem_relinquish();
   }
-  if (tid == 0) {
+  // The TMA thread initialises the barriers and starts the query loads before the CTA-wide
+  // barrier, so their latency overlaps the TMEM allocation and the other warps' start-up.
+  const bool tma_thread = (warp == 8 && lane == 0);
+  if (tma_thread) {
     mbar_init(BAR_QF, 1);
     for (int x = 0; x < 2; ++x) {
       mbar_init(BAR_QR(x), 128);
@@ -159,6 +162,15 @@ __global__ void __launch_bounds__(384, 1)
     *failed = 0;
     mbar_fence_init();
     fence_proxy_async_smem();
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    const int n_q = nkb > 0 ? 2 : 1;  // tile B is skipped when it lies past T
+    mbar_expect_tx(BAR_QF, n_q * S::Q_BYTES);
+    for (int x = 0; x < n_q; ++x)
+#pragma unroll
+      for (int blk = 0; blk < S::NBLK; ++blk)
+        tma_load_3d(sbase + (x ? S::OFF_QB : S::OFF_QA) + blk * BM * SPAN, &tm_q, BAR_QF,
+                    blk * (SPAN / 2), q0(x), bh);
   }
   tc_fence_before();
   __syncthreads();
@@ -219,23 +231,38 @@ __global__ void __launch_bounds__(384, 1)
         break;
       }
       tc_fence_after();
+      // S in two halves: the first half is masked and reduced while the second half loads.
       float s[BN];
+      const int k0 = j * BN;
+      const bool diag = k0 + BN - 1 > q0(x);  // tile crosses this query tile's diagonal
 #pragma unroll
-      for (int c = 0; c < BN; c += 16) tmem_ld16(s_addr + c, s + c);
+      for (int c = 0; c < BN / 2; c += 16) tmem_ld16(s_addr + c, s + c);
+      tmem_wait_ld();
+#pragma unroll
+      for (int c = BN / 2; c < BN; c += 16) tmem_ld16(s_addr + c, s + c);
+      if (diag) {
+#pragma unroll
+        for (int c = 0; c < BN / 2; ++c)
+          if (k0 + c > qrow) s[c] = -INFINITY;
+      }
+      float mq[4] = {fmaxf(s[0], s[1]), fmaxf(s[2], s[3]), fmaxf(s[4], s[5]), fmaxf(s[6], s[7])};
+#pragma unroll
+      for (int c = 8; c < BN / 2; c += 8) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) mq[i] = max3(mq[i], s[c + 2 * i], s[c + 2 * i + 1]);
+      }
       tmem_wait_ld();
       if constexpr (S::SEP_P) {
         tc_fence_before();
         mbar_arrive(BAR_SC(x));  // S is in registers: the next Q K^T may overwrite it
       }
-      const int k0 = j * BN;
-      if (k0 + BN - 1 > q0(x)) {  // tile crosses this query tile's diagonal
+      if (diag) {
 #pragma unroll
-        for (int c = 0; c < BN; ++c)
+        for (int c = BN / 2; c < BN; ++c)
           if (k0 + c > qrow) s[c] = -INFINITY;
       }
-      float mq[4] = {fmaxf(s[0], s[1]), fmaxf(s[2], s[3]), fmaxf(s[4], s[5]), fmaxf(s[6], s[7])};
 #pragma unroll
-      for (int c = 8; c < BN; c += 8) {
+      for (int c = BN / 2; c < BN; c += 8) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) mq[i] = max3(mq[i], s[c + 2 * i], s[c + 2 * i + 1]);
       }
@@ -322,16 +349,7 @@ __global__ void __launch_bounds__(384, 1)
     // ------------------------------------------------------------------ TMA: Q, then the K ring
     regs_dec<S::REG_OTHER>();
     if (lane == 0) {
-      tma_prefetch_desc(&tm_q);
-      tma_prefetch_desc(&tm_k);
-      const int n_q = nkb > 0 ? 2 : 1;  // tile B is skipped when it lies past T
-      mbar_expect_tx(BAR_QF, n_q * S::Q_BYTES);
-      for (int x = 0; x < n_q; ++x)
-#pragma unroll
-        for (int blk = 0; blk < S::NBLK; ++blk)
-          tma_load_3d(sbase + (x ? S::OFF_QB : S::OFF_QA) + blk * BM * SPAN, &tm_q, BAR_QF,
-                      blk * (SPAN / 2), q0(x), bh);
-      int issued = 0;
+      int issued = 0;  // (the query tiles were issued before the CTA barrier)
       for (int j = 0; j < nk_all; ++j) {
         const int s = j % NSK;
         if (j >= NSK && !mbar_wait(BAR_KE(s), (j / NSK - 1) & 1, failed, 310)) break;
