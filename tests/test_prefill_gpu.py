@@ -124,6 +124,29 @@ def test_prefill_llama_shape_long_context_sampled_rows(cuda_device):
     assert_no_device_timeouts()
 
 
+@pytest.mark.parametrize("T,D", [(4096, 64), (4097, 64), (6000, 64), (5000, 32)])
+def test_prefill_both_kernels_around_the_length_switch(cuda_device, T, D):
+    """Head_dim <= 64 runs one query tile per CTA up to T = 4096 and two tiles per CTA beyond;
+    both sides of the switch, ragged lengths included, against the oracle on sampled rows."""
+    B, Hq, Hkv = 1, 4, 2
+    dtype = torch.bfloat16
+    q = randn((B, Hq, T, D), 510 + T, dtype)
+    k = randn((B, Hkv, T, D), 511 + T, dtype)
+    v = randn((B, Hkv, T, D), 512 + T, dtype)
+    cos, sin = precompute_rope_cos_sin(T, D, "cpu", dtype)
+    out, lse = dominus_ultra_prefill(q.cuda(), k.cuda(), v.cuda(), cos.cuda(), sin.cuda(), Hkv)
+    torch.cuda.synchronize()
+    out, lse = out.cpu(), lse.cpu()
+    g = torch.Generator().manual_seed(513 + T)
+    rows = sorted(set(list(range(64)) + list(range(T - 200, T)) +
+                      torch.randint(0, T, (128,), generator=g).tolist()))
+    for h in (0, 3):
+        ro, rl = oracle.prefill_rows(q, k, v, cos, sin, Hkv, 0, h, rows)
+        assert max_abs(out[0, h, rows], ro) <= OUT_TOL
+        assert max_abs(lse[0, h, rows], rl) <= LSE_TOL
+    assert_no_device_timeouts()
+
+
 GOLDEN = np.load(Path(__file__).parent / "golden" / "golden.npz")
 
 
