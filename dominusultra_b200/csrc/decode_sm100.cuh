@@ -213,6 +213,8 @@ __global__ void __launch_bounds__(DecodeShape<D, GT>::NTHREADS, (GT == 1) ? 3 : 
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // The merge launched after this kernel may start its launch now; it waits for our completion.
+  if (threadIdx.x == 0) griddep_launch_dependents();
   if (threadIdx.x == 0) {
     for (int s = 0; s < NSTG; ++s) {
       mbar_init(FULL(s), 1);
@@ -577,6 +579,7 @@ __global__ void __launch_bounds__(128) merge_kernel(const float* __restrict__ o_
   __shared__ float w[MERGE_MAX_R];
   __shared__ float red[4];
   __shared__ float s_m, s_w;
+  griddep_wait();  // the partials' producer (when launched as its dependent) has completed
   const long long row = blockIdx.x;
   const int tid = threadIdx.x;
   float mx = -INFINITY;

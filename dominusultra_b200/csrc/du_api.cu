@@ -432,9 +432,23 @@ int launch_merge(const float* o_parts, const float* lse_parts, int R, int rows, 
                  long long o_sr, long long o_srow, long long l_sr, long long l_srow, void* out,
                  int out_kind, float* lse_out, cudaStream_t st) {
   if (R > du::MERGE_MAX_R) return fail(DU_ERR_UNSUPPORTED, "more partials than the merge supports");
-  du::merge_kernel<<<rows, 128, 0, st>>>(o_parts, lse_parts, R, D, o_sr, o_srow, l_sr, l_srow,
-                                             out, out_kind, lse_out);
-  cudaError_t e = cudaGetLastError();
+  // Launched as a programmatic dependent of the preceding kernel on the stream (the decode split
+  // kernel signals at its start), so the merge's launch and set-up overlap that kernel's tail;
+  // the merge waits for the producer's completion before reading the partials.
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(rows));
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, du::merge_kernel, o_parts, lse_parts, R, D, o_sr, o_srow,
+                                     l_sr, l_srow, out, out_kind, lse_out);
+  if (e != cudaSuccess) return cuda_fail(e, "merge launch");
+  e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "merge launch");
   return DU_OK;
 }

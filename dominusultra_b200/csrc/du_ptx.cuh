@@ -236,6 +236,15 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
+// Programmatic dependent launch: a kernel launched after this one with programmatic stream
+// serialization may be scheduled once every CTA of this grid has executed launch_dependents;
+// its griddep_wait then blocks until this grid has completed and its memory is visible (a no-op
+// for a kernel launched without the attribute).
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // True in exactly one lane of the (converged) warp: the lane that issues single-thread
 // tcgen05 operations while the whole warp walks the schedule.
 __device__ __forceinline__ bool elect_one() {

@@ -27,7 +27,7 @@
 #include "prefill_sm100.cuh"
 
 #ifndef DU_FA1_POLY_MASK
-#define DU_FA1_POLY_MASK 0x49
+#define DU_FA1_POLY_MASK 0x11
 #endif
 
 namespace du {
