@@ -14,6 +14,7 @@ from dominusultra_b200.attention import (  # noqa: F401
     _validate_head_dim,
     _validate_rope_tables,
     dominus_ultra_decode,
+    dominus_ultra_decode_kvcache,
     dominus_ultra_prefill,
     precompute_rope_cos_sin,
 )

@@ -48,6 +48,11 @@ SIGNATURES = {
         _i,
         [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _ll, _vp, _sz, _vp],
     ),
+    "du_decode_kvcache_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
+    "du_decode_kvcache": (
+        _i,
+        [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _ll, _vp, _sz, _vp],
+    ),
     "du_decode_partial": (
         _i,
         [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _ll, _ll, _ll, _vp, _sz, _vp],

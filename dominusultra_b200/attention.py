@@ -20,6 +20,7 @@ __all__ = [
     "precompute_rope_cos_sin",
     "dominus_ultra_prefill",
     "dominus_ultra_decode",
+    "dominus_ultra_decode_kvcache",
     "decode_partial",
     "merge_partials",
 ]
@@ -293,6 +294,120 @@ def dominus_ultra_decode(
             min(cos.shape[0], sin.shape[0]), ws, nbytes, stream,
         )
     _lib.check(rc, "du_decode")
+    return out.unsqueeze(2)
+
+
+def dominus_ultra_decode_kvcache(
+    q_new: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    cos: torch.Tensor,
+    sin: torch.Tensor,
+    cache_seqlens: torch.Tensor,
+    k_new: Optional[torch.Tensor] = None,
+    v_new: Optional[torch.Tensor] = None,
+    num_kv_heads: Optional[int] = None,
+) -> torch.Tensor:
+    """
+    One decode step of a generation loop: per-sequence cache lengths, new token appended.
+
+    The caller step around ``dominus_ultra_decode`` (``dominus_ultra.py:504-583``), which takes
+    one length for the whole batch and attends to the cache without the current token
+    (``dominus_ultra.py:350``). Here ``k_cache`` / ``v_cache`` are preallocated to a capacity
+    ``max_len`` and sequence ``b`` holds ``s_b = cache_seqlens[b]`` tokens:
+
+    * with ``k_new`` / ``v_new`` (``[batch, num_kv_heads, 1, head_dim]``) the new token's key
+      and value are written in place to row ``s_b`` of the caches, and the query attends to
+      keys ``0..s_b`` (itself included);
+    * without them the query attends to keys ``0..s_b-1`` (``dominus_ultra_decode`` of that
+      prefix).
+
+    The query rotates at position ``s_b`` and cached key ``j`` at ``j``. ``cache_seqlens`` is
+    not advanced (the caller adds 1 after an append). When it is a CUDA tensor it is read on
+    the GPU: the call never synchronises, and a captured CUDA graph stays valid as the lengths
+    change. A length out of range (``s_b < 0`` or ``s_b + 1 > max_len`` with an append) cannot
+    raise without a sync: that sequence's output is zero, nothing is appended, and
+    ``_lib.read_status()`` reports code 6. A CPU ``cache_seqlens`` is checked here instead.
+
+    Args:
+        q_new: [batch, num_heads, 1, head_dim]
+        k_cache, v_cache: [batch, num_kv_heads, max_len, head_dim], contiguous, updated in place
+        cos, sin: tables from precompute_rope_cos_sin covering max_len positions (max_len + 1
+            without an append)
+        cache_seqlens: [batch] integer tokens already cached per sequence
+        k_new, v_new: [batch, num_kv_heads, 1, head_dim] or None (both)
+        num_kv_heads: Number of KV heads for GQA. If None, uses num_query_heads (MHA)
+
+    Returns:
+        Output tensor of shape [batch, num_heads, 1, head_dim]
+    """
+    if q_new.ndim != 4 or k_cache.ndim != 4 or v_cache.ndim != 4:
+        raise ValueError("q_new, k_cache, and v_cache must be rank-4 tensors")
+    if (k_new is None) != (v_new is None):
+        raise ValueError("k_new and v_new must be given together")
+    append = k_new is not None
+    B, Hq, _, D = q_new.shape
+    _, Hk, max_len, _ = k_cache.shape
+    KvH = num_kv_heads if num_kv_heads is not None else Hq
+    if q_new.shape[2] != 1:
+        raise ValueError("q_new must contain exactly one sequence position")
+    if B <= 0 or Hq <= 0 or max_len <= 0:
+        raise ValueError("batch, heads, and cache length must be positive")
+    if KvH <= 0 or Hq % KvH != 0:
+        raise ValueError("num_query_heads must be divisible by num_kv_heads")
+    if k_cache.shape != (B, KvH, max_len, D) or v_cache.shape != (B, KvH, max_len, D):
+        raise ValueError("k_cache and v_cache must have matching GQA cache shapes")
+    if Hk != KvH:
+        raise ValueError("cache head count does not match num_kv_heads")
+    if append and (k_new.shape != (B, KvH, 1, D) or v_new.shape != (B, KvH, 1, D)):
+        raise ValueError("k_new and v_new must have shape [batch, num_kv_heads, 1, head_dim]")
+    if cache_seqlens.ndim != 1 or cache_seqlens.shape[0] != B:
+        raise ValueError("cache_seqlens must have shape [batch]")
+    if cache_seqlens.dtype not in (torch.int32, torch.int64):
+        raise ValueError("cache_seqlens must be an int32 or int64 tensor")
+
+    _validate_head_dim(D)
+    tensors = (q_new, k_cache, v_cache) + ((k_new, v_new) if append else ())
+    _validate_attention_tensors(*tensors)
+    _validate_rope_tables(cos, sin, max_len + (0 if append else 1), D, q_new.device, q_new.dtype)
+    if k_cache.data_ptr() % 16 or v_cache.data_ptr() % 16:
+        raise ValueError("k_cache and v_cache must be 16-byte aligned (they are updated in place)")
+    if cache_seqlens.device.type == "cpu":
+        lens = cache_seqlens.tolist()
+        hi = max_len - (1 if append else 0)
+        bad = [i for i, s in enumerate(lens) if s < 0 or s > hi]
+        if bad:
+            raise ValueError(
+                f"cache_seqlens[{bad[0]}] = {lens[bad[0]]} is outside [0, {hi}] "
+                f"for a cache of {max_len} positions" + (" with an append" if append else "")
+            )
+        cache_seqlens = cache_seqlens.to(q_new.device)
+    elif cache_seqlens.device != q_new.device:
+        raise ValueError("cache_seqlens must be on the device of q_new (or on the CPU)")
+    if cache_seqlens.dtype != torch.int32:
+        cache_seqlens = cache_seqlens.to(torch.int32)
+    seqlens = cache_seqlens.contiguous()
+
+    lib = _lib.load()
+    q_new, cos, sin = (_aligned(t) for t in (q_new, cos, sin))
+    if append:
+        k_new, v_new = _aligned(k_new), _aligned(v_new)
+    out = torch.empty_like(q_new).squeeze(2)
+    scale = 1.0 / (D**0.5)
+    with _OnDevice(q_new.device):
+        stream = _stream(q_new.device)
+        ws, nbytes = _cached_workspace(
+            "decode_kvcache",
+            int(lib.du_decode_kvcache_workspace_size(B, Hq, KvH, max_len, D)),
+            q_new.device,
+            stream,
+        )
+        rc = lib.du_decode_kvcache(
+            _ptr(q_new), _ptr(k_new), _ptr(v_new), _ptr(k_cache), _ptr(v_cache), _ptr(seqlens),
+            _ptr(cos), _ptr(sin), _ptr(out), B, Hq, KvH, max_len, D, _dtype_code(q_new.dtype),
+            scale, min(cos.shape[0], sin.shape[0]), ws, nbytes, stream,
+        )
+    _lib.check(rc, "du_decode_kvcache")
     return out.unsqueeze(2)
 
 

@@ -56,12 +56,28 @@ struct DecodeParams {
   long long kv_pos_offset;
   float scale_log2;
   int mode;  // 0: final output in dtype (n_split == 1); 1: fp32 partials
+  // Per-sequence cache lengths (varlen != 0), prepared by decode_prep_kernel on the same stream:
+  // pre[b] is the flattened chunk index where sequence b's units start (pre[B] = total), lenq[b]
+  // = {keys attended, query position}. Partials go to fragment slots: fragment (unit u, CTA c)
+  // writes rows (u + c) * GT + gg of o_part / lse_part (u + c grows along the flattened order,
+  // so every fragment has its own slot).
+  const long long* pre;
+  const int2* lenq;
+  int B;
+  int ub;  // units per sequence: Hkv * n_gchunk
+  int varlen;
 };
 
-// One fragment of a CTA's work: keys [kbeg, kend) of one unit, written to partial slot `slot`.
+// Fewest chunks a CTA takes in the per-sequence-length walk: one-chunk fragments would cost
+// more in partials than they balance.
+constexpr int DECODE_VARLEN_MIN_PER = 2;
+
+// One fragment of a CTA's work: keys [kbeg, kend) of one unit, written to partial slot `slot`,
+// with the query at position qpos.
 struct DecodeFrag {
   int unit, kbeg, kend, slot;
   bool last;  // the unit's last fragment
+  long long qpos;
 };
 
 // The CTA's work, walked identically by its producer and consumers. With one slot per row, whole
@@ -71,7 +87,29 @@ struct DecodeFrag {
 // the first of them writing slot 0.
 struct DecodeWalk {
   long long cur, hi;
+  long long per;  // per-sequence lengths: chunks per CTA
+  int b;          // per-sequence lengths: the sequence holding chunk `cur`
+  // Chunks per CTA of the per-sequence-length walk; decode_merge_varlen_kernel uses the same.
+  __device__ __forceinline__ static long long varlen_per(long long total, long long grid) {
+    const long long per = (total + grid - 1) / grid;
+    return per > DECODE_VARLEN_MIN_PER ? per : DECODE_VARLEN_MIN_PER;
+  }
   __device__ __forceinline__ void init(const DecodeParams& p) {
+    if (p.varlen) {
+      // Equal ranges of the flattened chunks that are actually present (pre[B] of them).
+      const long long total = p.pre[p.B];
+      per = varlen_per(total, gridDim.x);
+      cur = static_cast<long long>(blockIdx.x) * per;
+      hi = min(total, cur + per);
+      int lo = 0, up = p.B;  // pre[lo] <= cur < pre[up]
+      if (cur < hi)
+        while (up - lo > 1) {
+          const int mid = (lo + up) >> 1;
+          if (p.pre[mid] <= cur) lo = mid; else up = mid;
+        }
+      b = lo;
+      return;
+    }
     if (p.n_split == 1) {
       cur = blockIdx.x;
       hi = p.n_units;
@@ -89,6 +127,25 @@ struct DecodeWalk {
   }
   __device__ __forceinline__ bool next(const DecodeParams& p, int CK, DecodeFrag& f) {
     if (cur >= hi) return false;
+    if (p.varlen) {
+      while (p.pre[b + 1] <= cur) ++b;  // every sequence has at least one chunk per unit
+      const long long base = p.pre[b];
+      const long long nb = (p.pre[b + 1] - base) / p.ub;  // chunks per unit of sequence b
+      const long long ui = (cur - base) / nb;
+      const long long ub = base + ui * nb;
+      const long long e = min(hi, ub + nb);
+      const int2 lq = p.lenq[b];
+      f.unit = b * p.ub + static_cast<int>(ui);
+      f.kbeg = static_cast<int>(cur - ub) * CK;
+      f.kend = min(lq.x, static_cast<int>(e - ub) * CK);
+      if (f.kend < f.kbeg) f.kend = f.kbeg;  // an empty sequence: one fragment with no keys
+      f.slot = f.unit + static_cast<int>(blockIdx.x);
+      f.last = (e == ub + nb);
+      f.qpos = lq.y;
+      cur = e;
+      return true;
+    }
+    f.qpos = p.q_pos;
     if (p.n_split == 1) {
       f.unit = static_cast<int>(cur);
       f.kbeg = 0;
@@ -231,6 +288,12 @@ __global__ void __launch_bounds__(DecodeShape<D, GT>::NTHREADS, (GT == 1) ? 3 : 
     fence_proxy_async_smem();
   }
   __syncthreads();
+  // Per-sequence lengths: the prep kernel (this launch's programmatic predecessor) has written
+  // the chunk offsets and the appended cache rows once this returns.
+  if (p.varlen) {
+    griddep_wait();
+    fence_proxy_async_global();  // the appended rows are read by TMA (async proxy)
+  }
 
   const uint8_t* cosb = static_cast<const uint8_t*>(p.cos);
   const uint8_t* sinb = static_cast<const uint8_t*>(p.sin);
@@ -264,7 +327,7 @@ __global__ void __launch_bounds__(DecodeShape<D, GT>::NTHREADS, (GT == 1) ? 3 : 
           const int b = bk / p.Hkv;
           const int h0 = (bk - b * p.Hkv) * p.G + gch * GT;
           const uint32_t hd = sbase + S::OFF_HDR + hs * S::HDR;
-          const size_t trow = static_cast<size_t>(p.q_pos) * S::TABB;
+          const size_t trow = static_cast<size_t>(fr.qpos) * S::TABB;
           mbar_expect_tx(HFULL(hs), static_cast<uint32_t>(S::HDR_Q + 2 * S::TABB));
           bulk_load(hd, static_cast<const uint8_t*>(p.q) + (static_cast<size_t>(b) * p.Hq + h0) * S::ROWB,
                     S::HDR_Q, HFULL(hs));
@@ -539,7 +602,11 @@ __global__ void __launch_bounds__(DecodeShape<D, GT>::NTHREADS, (GT == 1) ? 3 : 
       }
       const size_t row = static_cast<size_t>(b) * p.Hq + h0 + gg;
       const float val = (Lsum > 0.f) ? A / Lsum : 0.f;
-      if (p.mode == 0) {
+      if (p.varlen) {
+        const size_t fs = static_cast<size_t>(split) * GT + gg;  // fragment slot row
+        p.o_part[fs * D + d] = val;
+        if (d == 0) p.lse_part[fs] = (Lsum > 0.f) ? (M + lg2(Lsum)) * 0.69314718055994531f : -INFINITY;
+      } else if (p.mode == 0) {
         if constexpr (BF16) {
           static_cast<__nv_bfloat16*>(p.out)[row * D + d] = __float2bfloat16_rn(val);
         } else {
@@ -564,27 +631,19 @@ __global__ void __launch_bounds__(DecodeShape<D, GT>::NTHREADS, (GT == 1) ? 3 : 
   }
 }
 
-// LSE-weighted merge of R partials per row: lse = log(sum_r exp(lse_r)),
-// out = sum_r exp(lse_r - lse) * o_r. Rows whose partials all have lse = -inf produce zeros and
-// lse = -inf. out_kind: 0 fp16, 1 bf16, 2 fp32. One CTA per row: the R weights are computed in
-// parallel into shared memory (R <= MERGE_MAX_R), then each thread sums its columns with
-// independent loads.
 constexpr int MERGE_MAX_R = 4096;
 
-__global__ void __launch_bounds__(128) merge_kernel(const float* __restrict__ o_parts,
-                                                    const float* __restrict__ lse_parts, int R,
-                                                    int D, long long o_sr, long long o_srow,
-                                                    long long l_sr, long long l_srow, void* out,
-                                                    int out_kind, float* lse_out) {
-  __shared__ float w[MERGE_MAX_R];
+// Body of the merges: one CTA of 128 threads combines the R partials of one row, partial r at
+// lse[r * l_sr] and o[r * o_sr + d]; `w` is a shared array of at least R floats.
+__device__ __forceinline__ void merge_row(const float* __restrict__ o, const float* __restrict__ lse,
+                                          int R, int D, long long o_sr, long long l_sr, void* out,
+                                          int out_kind, float* lse_out, long long row, float* w) {
   __shared__ float red[4];
   __shared__ float s_m, s_w;
-  griddep_wait();  // the partials' producer (when launched as its dependent) has completed
-  const long long row = blockIdx.x;
   const int tid = threadIdx.x;
   float mx = -INFINITY;
   for (int r = tid; r < R; r += 128) {
-    const float v = lse_parts[r * l_sr + row * l_srow];
+    const float v = lse[r * l_sr];
     w[r] = v;
     mx = fmaxf(mx, v);
   }
@@ -611,7 +670,7 @@ __global__ void __launch_bounds__(128) merge_kernel(const float* __restrict__ o_
   const float W = s_w;
   const float inv = (W > 0.f) ? 1.0f / W : 0.f;
   for (int d = tid; d < D; d += 128) {
-    const float* src = o_parts + row * o_srow + d;
+    const float* src = o + d;
     float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
     int r = 0;
     for (; r + 4 <= R; r += 4) {
@@ -632,6 +691,130 @@ __global__ void __launch_bounds__(128) merge_kernel(const float* __restrict__ o_
     }
   }
   if (lse_out != nullptr && tid == 0) lse_out[row] = (W > 0.f) ? M + logf(W) : -INFINITY;
+}
+
+// LSE-weighted merge of R partials per row: lse = log(sum_r exp(lse_r)),
+// out = sum_r exp(lse_r - lse) * o_r. Rows whose partials all have lse = -inf produce zeros and
+// lse = -inf. out_kind: 0 fp16, 1 bf16, 2 fp32. One CTA per row: the R weights are computed in
+// parallel into shared memory (R <= MERGE_MAX_R), then each thread sums its columns with
+// independent loads.
+__global__ void __launch_bounds__(128) merge_kernel(const float* __restrict__ o_parts,
+                                                    const float* __restrict__ lse_parts, int R,
+                                                    int D, long long o_sr, long long o_srow,
+                                                    long long l_sr, long long l_srow, void* out,
+                                                    int out_kind, float* lse_out) {
+  __shared__ float w[MERGE_MAX_R];
+  griddep_wait();  // the partials' producer (when launched as its dependent) has completed
+  const long long row = blockIdx.x;
+  merge_row(o_parts + row * o_srow, lse_parts + row * l_srow, R, D, o_sr, l_sr, out, out_kind,
+            lse_out, row, w);
+}
+
+// ------------------------------------------------------------------------------------------
+// Per-sequence cache lengths with the new token's K/V appended (decode over a KV cache as a
+// generation loop holds it).
+// ------------------------------------------------------------------------------------------
+struct DecodePrepParams {
+  const int* seqlens;  // [B] tokens in each sequence's cache before this step
+  const void* k_new;   // [B, Hkv, D] the new token's key / value, or nullptr (no append)
+  const void* v_new;
+  void* k_cache;       // [B, Hkv, L, D]
+  void* v_cache;
+  long long* pre;      // out [B + 1]: flattened chunk offsets (DecodeParams::pre)
+  int2* lenq;          // out [B]: {keys attended, query position}
+  int B, Hkv, L, D, CK, ub, append;
+  long long rope_positions;
+};
+
+// A cache length s is usable when 0 <= s, the append fits (s + append <= L) and the tables hold
+// the query position s. Anything else is recorded (status code 6) and the sequence is treated
+// as empty: no append, no keys, zero output.
+__device__ __forceinline__ bool decode_len_ok(const DecodePrepParams& p, int s) {
+  return s >= 0 && s + p.append <= p.L && static_cast<long long>(s) < p.rope_positions;
+}
+
+// CTA 0 scans the per-sequence chunk counts into pre / lenq; every CTA copies its share of the
+// new K / V rows (16 bytes per thread step) into row seqlens[b] of the caches.
+__global__ void __launch_bounds__(256) decode_prep_kernel(const DecodePrepParams p) {
+  griddep_launch_dependents();  // the split kernel may launch; it waits for this grid's writes
+  __shared__ long long warp_tot[8];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (blockIdx.x == 0) {
+    long long carry = 0;
+    for (int base = 0; base < p.B; base += 256) {
+      const int b = base + tid;
+      long long x = 0;
+      if (b < p.B) {
+        const int s = p.seqlens[b];
+        const bool ok = decode_len_ok(p, s);
+        if (!ok) record_error(6u, static_cast<unsigned>(b), static_cast<unsigned>(s));
+        const int len = ok ? s + p.append : 0;
+        p.lenq[b] = make_int2(len, ok ? s : 0);
+        const int nch = (len + p.CK - 1) / p.CK;
+        x = static_cast<long long>(p.ub) * (nch > 1 ? nch : 1);
+      }
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const long long y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+      }
+      if (lane == 31) warp_tot[warp] = x;
+      __syncthreads();
+      long long before = carry, tot = 0;
+#pragma unroll
+      for (int w2 = 0; w2 < 8; ++w2) {
+        if (w2 < warp) before += warp_tot[w2];
+        tot += warp_tot[w2];
+      }
+      if (b < p.B) p.pre[b + 1] = before + x;
+      carry += tot;
+      __syncthreads();
+    }
+    if (tid == 0) p.pre[0] = 0;
+  }
+  if (p.append) {
+    const int cpr = p.D / 8;  // 16-byte pieces per row
+    const long long n = static_cast<long long>(p.B) * p.Hkv * cpr;
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + tid; i < n;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+      const long long r = i / cpr;  // b * Hkv + kv head
+      const int c = static_cast<int>(i - r * cpr);
+      const int s = p.seqlens[r / p.Hkv];
+      if (!decode_len_ok(p, s)) continue;
+      const long long dst = (r * p.L + s) * cpr + c;
+      reinterpret_cast<uint4*>(p.k_cache)[dst] = reinterpret_cast<const uint4*>(p.k_new)[i];
+      reinterpret_cast<uint4*>(p.v_cache)[dst] = reinterpret_cast<const uint4*>(p.v_new)[i];
+    }
+  }
+}
+
+// Merge of the fragment slots of the per-sequence-length walk: one CTA per (b, query head).
+// The row's unit u spans the CTAs c0..c1 of the walk (same chunk offsets and chunks per CTA as
+// DecodeWalk); fragment (u, c) wrote row (u + c) * GT + gg.
+__global__ void __launch_bounds__(128) decode_merge_varlen_kernel(
+    const float* __restrict__ o_parts, const float* __restrict__ lse_parts,
+    const long long* __restrict__ pre, int Hq, int Hkv, int GT, int ub, int B, int D,
+    int split_grid, void* out, int out_kind) {
+  __shared__ float w[MERGE_MAX_R];
+  griddep_wait();  // the split kernel has completed
+  const long long row = blockIdx.x;  // b * Hq + h
+  const int b = static_cast<int>(row / Hq);
+  const int h = static_cast<int>(row - static_cast<long long>(b) * Hq);
+  const int G = Hq / Hkv;
+  const int kvh = h / G;
+  const int gch = (h - kvh * G) / GT;
+  const int gg = h - kvh * G - gch * GT;
+  const int ui = kvh * (G / GT) + gch;  // unit within the sequence
+  const long long base = pre[b];
+  const long long nb = (pre[b + 1] - base) / ub;
+  const long long start = base + ui * nb;
+  const long long per = DecodeWalk::varlen_per(pre[B], split_grid);
+  const long long c0 = start / per;
+  const long long c1 = (start + nb - 1) / per;
+  const long long u = static_cast<long long>(b) * ub + ui;
+  const long long slot0 = (u + c0) * GT + gg;
+  merge_row(o_parts + slot0 * D, lse_parts + slot0, static_cast<int>(c1 - c0 + 1), D,
+            static_cast<long long>(GT) * D, GT, out, out_kind, nullptr, row, w);
 }
 
 }  // namespace du

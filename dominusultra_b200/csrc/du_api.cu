@@ -381,6 +381,24 @@ size_t decode_ws_bytes(const DecodePlan& pl, int B, int Hq, int D) {
   return ((o + 255) / 256) * 256 + l;
 }
 
+// Launch on `st`; with `pdl` as a programmatic dependent of the stream's previous kernel (the
+// kernel must call griddep_wait before touching that kernel's outputs).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kern)(KArgs...), unsigned grid, unsigned block, size_t smem,
+                          cudaStream_t st, bool pdl, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 template <int D, bool BF16, int GT>
 int launch_decode_split_t(const du::DecodeParams& prm, int B, long long rope_positions, int grid,
                           cudaStream_t st) {
@@ -398,8 +416,11 @@ int launch_decode_split_t(const du::DecodeParams& prm, int B, long long rope_pos
   auto kern = du::decode_kernel<D, BF16, GT>;
   cudaError_t e = ensure_smem_attr(kern, S::SMEM_BYTES);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(decode)");
-  // The work walk depends on the grid size the plan chose (resident CTAs only).
-  kern<<<static_cast<unsigned>(grid), S::NTHREADS, S::SMEM_BYTES, st>>>(tk, tv, tc, ts, prm);
+  // The work walk depends on the grid size the plan chose (resident CTAs only). With per-sequence
+  // lengths the kernel follows decode_prep_kernel as its programmatic dependent.
+  e = launch_kernel(kern, static_cast<unsigned>(grid), S::NTHREADS, S::SMEM_BYTES, st,
+                    prm.varlen != 0, tk, tv, tc, ts, prm);
+  if (e != cudaSuccess) return cuda_fail(e, "decode launch");
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "decode launch");
   return DU_OK;
@@ -435,18 +456,9 @@ int launch_merge(const float* o_parts, const float* lse_parts, int R, int rows, 
   // Launched as a programmatic dependent of the preceding kernel on the stream (the decode split
   // kernel signals at its start), so the merge's launch and set-up overlap that kernel's tail;
   // the merge waits for the producer's completion before reading the partials.
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(static_cast<unsigned>(rows));
-  cfg.blockDim = dim3(128);
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, du::merge_kernel, o_parts, lse_parts, R, D, o_sr, o_srow,
-                                     l_sr, l_srow, out, out_kind, lse_out);
+  cudaError_t e = launch_kernel(du::merge_kernel, static_cast<unsigned>(rows), 128, 0, st, true,
+                                o_parts, lse_parts, R, D, o_sr, o_srow, l_sr, l_srow, out,
+                                out_kind, lse_out);
   if (e != cudaSuccess) return cuda_fail(e, "merge launch");
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "merge launch");
@@ -532,6 +544,115 @@ int decode_impl(const void* q, const void* kc, const void* vc, const void* cos, 
   return launch_merge(o_part, l_part, pl.n_split, static_cast<int>(rows), D, D,
                       static_cast<long long>(pl.n_split) * D, 1, pl.n_split, out_f32, DU_DTYPE_F32,
                       lse_f32, st);
+}
+
+// Workspace of du_decode_kvcache: chunk offsets [B + 1] (int64), {len, qpos} [B] (int2), then
+// the fragment-slot partials, o [(units + grid) * GT, D] and lse [(units + grid) * GT] fp32.
+struct KvcacheLayout {
+  size_t pre, lenq, o, lse, total;
+};
+
+KvcacheLayout kvcache_layout(const DecodePlan& pl, int B, int D, int grid) {
+  auto up = [](size_t x) { return ((x + 255) / 256) * 256; };
+  KvcacheLayout ly{};
+  const size_t slots = (static_cast<size_t>(pl.n_units) + grid) * pl.GT;
+  ly.pre = 0;
+  ly.lenq = up(sizeof(long long) * (static_cast<size_t>(B) + 1));
+  ly.o = ly.lenq + up(sizeof(int) * 2 * static_cast<size_t>(B));
+  ly.lse = ly.o + up(slots * D * sizeof(float));
+  ly.total = ly.lse + slots * sizeof(float);
+  return ly;
+}
+
+int kvcache_grid(const DecodePlan& pl) { return sm_count() * decode_residency(pl.GT); }
+
+int decode_kvcache_impl(const void* q, const void* k_new, const void* v_new, void* kc, void* vc,
+                        const int* seqlens, const void* cos, const void* sin, void* out, int B,
+                        int Hq, int Hkv, int L, int D, int dtype, float scale,
+                        long long rope_positions, void* ws, size_t ws_bytes, cudaStream_t st) {
+  int rc = check_common(B, Hq, Hkv, L, D, dtype);
+  if (rc != DU_OK) return rc;
+  if (!q || !kc || !vc || !seqlens || !cos || !sin || !out)
+    return fail(DU_ERR_INVALID, "null pointer argument");
+  if ((k_new == nullptr) != (v_new == nullptr))
+    return fail(DU_ERR_INVALID, "k_new and v_new must be given together");
+  const bool append = k_new != nullptr;
+  if (!aligned16(q) || !aligned16(kc) || !aligned16(vc) || !aligned16(cos) || !aligned16(sin) ||
+      (append && (!aligned16(k_new) || !aligned16(v_new))))
+    return fail(DU_ERR_INVALID, "q, k_new, v_new, caches and rope tables must be 16-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(seqlens) & 3u) != 0)
+    return fail(DU_ERR_INVALID, "cache_seqlens must be 4-byte aligned");
+  if (rope_positions < 1) return fail(DU_ERR_INVALID, "rope tables must have at least one row");
+  if (!(scale > 0.f)) return fail(DU_ERR_INVALID, "scale must be positive");
+  const DecodePlan pl = plan_decode(B, Hq, Hkv, L, D);
+  const int grid = kvcache_grid(pl);
+  const KvcacheLayout ly = kvcache_layout(pl, B, D, grid);
+  if (ws == nullptr || ws_bytes < ly.total || (reinterpret_cast<uintptr_t>(ws) & 255u) != 0)
+    return fail(DU_ERR_WORKSPACE, "decode_kvcache workspace of " + std::to_string(ly.total) +
+                                      " bytes (256-byte aligned) is required");
+  uint8_t* w8 = static_cast<uint8_t*>(ws);
+  du::DecodePrepParams pp{};
+  pp.seqlens = seqlens;
+  pp.k_new = k_new;
+  pp.v_new = v_new;
+  pp.k_cache = kc;
+  pp.v_cache = vc;
+  pp.pre = reinterpret_cast<long long*>(w8 + ly.pre);
+  pp.lenq = reinterpret_cast<int2*>(w8 + ly.lenq);
+  pp.B = B;
+  pp.Hkv = Hkv;
+  pp.L = L;
+  pp.D = D;
+  pp.CK = decode_chunk(D, pl.GT);
+  pp.ub = Hkv * pl.n_gchunk;
+  pp.append = append ? 1 : 0;
+  pp.rope_positions = rope_positions;
+  // One CTA scans the lengths; the append spreads over enough CTAs for a 16-byte piece each.
+  const long long pieces = append ? static_cast<long long>(B) * Hkv * (D / 8) : 0;
+  long long pgrid = (pieces + 255) / 256;
+  if (pgrid < 1) pgrid = 1;
+  if (pgrid > 2LL * sm_count()) pgrid = 2LL * sm_count();
+  cudaError_t e = launch_kernel(du::decode_prep_kernel, static_cast<unsigned>(pgrid), 256, 0, st,
+                                false, pp);
+  if (e != cudaSuccess) return cuda_fail(e, "decode prep launch");
+  du::DecodeParams prm{};
+  prm.q = q;
+  prm.k = kc;
+  prm.v = vc;
+  prm.cos = cos;
+  prm.sin = sin;
+  prm.Hq = Hq;
+  prm.Hkv = Hkv;
+  prm.L = L;
+  prm.G = Hq / Hkv;
+  prm.n_gchunk = pl.n_gchunk;
+  prm.n_split = 2;  // partials are written; slots come from the fragment walk
+  prm.n_units = pl.n_units;
+  prm.cpu = 0;
+  prm.total_chunks = 0;
+  prm.q_pos = 0;
+  prm.kv_pos_offset = 0;
+  prm.scale_log2 = scale * 1.4426950408889634f;
+  prm.mode = 1;
+  prm.o_part = reinterpret_cast<float*>(w8 + ly.o);
+  prm.lse_part = reinterpret_cast<float*>(w8 + ly.lse);
+  prm.pre = pp.pre;
+  prm.lenq = pp.lenq;
+  prm.B = B;
+  prm.ub = pp.ub;
+  prm.varlen = 1;
+  const bool bf16 = dtype == DU_DTYPE_BF16;
+  rc = bf16 ? launch_decode_split_d<true>(prm, pl.GT, D, B, rope_positions, grid, st)
+            : launch_decode_split_d<false>(prm, pl.GT, D, B, rope_positions, grid, st);
+  if (rc != DU_OK) return rc;
+  e = launch_kernel(du::decode_merge_varlen_kernel, static_cast<unsigned>(static_cast<long long>(B) * Hq),
+                    128, 0, st, true, static_cast<const float*>(prm.o_part),
+                    static_cast<const float*>(prm.lse_part), static_cast<const long long*>(pp.pre),
+                    Hq, Hkv, pl.GT, pp.ub, B, D, grid, out, dtype);
+  if (e != cudaSuccess) return cuda_fail(e, "decode merge launch");
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "decode merge launch");
+  return DU_OK;
 }
 
 }  // namespace
@@ -637,6 +758,23 @@ int du_decode(const void* q, const void* k_cache, const void* v_cache, const voi
   return decode_impl(q, k_cache, v_cache, cos, sin, out, nullptr, nullptr, B, Hq, Hkv, L, D,
                      dtype, scale, L, 0, rope_positions, workspace, workspace_bytes,
                      static_cast<cudaStream_t>(stream));
+}
+
+size_t du_decode_kvcache_workspace_size(int B, int Hq, int Hkv, int L, int D) {
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || L <= 0 || Hq % Hkv != 0 || !valid_head_dim(D)) return 0;
+  const DecodePlan pl = plan_decode(B, Hq, Hkv, L, D);
+  return kvcache_layout(pl, B, D, kvcache_grid(pl)).total;
+}
+
+int du_decode_kvcache(const void* q, const void* k_new, const void* v_new, void* k_cache,
+                      void* v_cache, const int* cache_seqlens, const void* cos, const void* sin,
+                      void* out, int B, int Hq, int Hkv, int L, int D, int dtype, float scale,
+                      long long rope_positions, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+  g_last_error.clear();
+  return decode_kvcache_impl(q, k_new, v_new, k_cache, v_cache, cache_seqlens, cos, sin, out, B,
+                             Hq, Hkv, L, D, dtype, scale, rope_positions, workspace,
+                             workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 int du_decode_partial(const void* q, const void* k_shard, const void* v_shard, const void* cos,

@@ -17,8 +17,9 @@
 #define DU_WAIT_TIMEOUT_NS 2000000000ull  // 2 s: far above any legitimate wait in these kernels
 #endif
 
-// Status words written by device code when a bounded wait expires:
-// [0] error code (0 ok, 5 timeout), [1] wait-site id, [2] blockIdx.x, [3] blockIdx.y.
+// Status words written by device code (the first error wins until the host resets them):
+//   code 5, a bounded wait expired: [1] wait-site id, [2] blockIdx.x, [3] blockIdx.y;
+//   code 6, a per-sequence cache length out of range: [1] sequence index, [2] the length.
 __device__ unsigned int g_du_status[4];
 
 namespace du {
@@ -38,6 +39,15 @@ __device__ __forceinline__ void record_timeout(unsigned int site) {
     g_du_status[1] = site;
     g_du_status[2] = blockIdx.x;
     g_du_status[3] = blockIdx.y;
+    __threadfence();
+  }
+}
+
+__device__ __forceinline__ void record_error(unsigned int code, unsigned int a, unsigned int b) {
+  if (atomicCAS(&g_du_status[0], 0u, code) == 0u) {
+    g_du_status[1] = a;
+    g_du_status[2] = b;
+    g_du_status[3] = 0u;
     __threadfence();
   }
 }
@@ -174,6 +184,12 @@ __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity, u
 // (tensor-core operand reads, TMA).
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Order global-memory data seen through the generic proxy before this thread's later
+// async-proxy (TMA) reads of global memory.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
 // ---------------------------------------------------------------------------------------------

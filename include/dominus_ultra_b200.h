@@ -28,6 +28,7 @@ extern "C" {
 #define DU_ERR_CUDA 3        /* a CUDA runtime / driver call failed */
 #define DU_ERR_WORKSPACE 4   /* workspace missing or too small */
 #define DU_ERR_TIMEOUT 5     /* a bounded device-side wait expired (see du_read_status) */
+#define DU_STATUS_BAD_SEQLEN 6 /* device status only: a per-sequence cache length out of range */
 
 #define DU_DTYPE_F16 0
 #define DU_DTYPE_BF16 1
@@ -90,6 +91,34 @@ int du_decode(const void* q, const void* k_cache, const void* v_cache, const voi
               void* stream);
 
 /*
+ * Workspace bytes du_decode_kvcache needs for these sizes on the current device (never 0).
+ */
+size_t du_decode_kvcache_workspace_size(int B, int Hq, int Hkv, int L, int D);
+
+/*
+ * Decode step of a generation loop over a KV cache of capacity L with per-sequence lengths,
+ * optionally appending the new token's key and value first (no counterpart in the reference:
+ * its decode_kernel, dominus_ultra.py:288-413, takes one length for every sequence, the whole
+ * cache, and excludes the current token, :350). cache_seqlens [B] int32 on the device holds the
+ * tokens already cached per sequence, s_b; it is read on the device, so the call never
+ * synchronises and a captured CUDA graph stays valid as the lengths grow.
+ *   - k_new, v_new [B, Hkv, D] (or both NULL): when given, written to row s_b of k_cache /
+ *     v_cache, and the query attends to keys 0..s_b; otherwise to keys 0..s_b-1.
+ *   - The query rotates at position s_b, cached key j at position j (as du_decode with L = s_b).
+ *   - q [B, Hq, D], caches [B, Hkv, L, D] (written only at row s_b), out [B, Hq, D].
+ *   - A sequence needs 0 <= s_b, s_b + (k_new != NULL) <= L and s_b < rope_positions. A
+ *     length outside that is not an argument error (the host never sees it): the sequence is
+ *     treated as empty (zero output, nothing appended) and du_read_status reports code 6 with
+ *     the sequence index and the length. An empty sequence without an append gives zeros.
+ * workspace: du_decode_kvcache_workspace_size bytes, 256-byte aligned.
+ */
+int du_decode_kvcache(const void* q, const void* k_new, const void* v_new, void* k_cache,
+                      void* v_cache, const int* cache_seqlens, const void* cos, const void* sin,
+                      void* out, int B, int Hq, int Hkv, int L, int D, int dtype, float scale,
+                      long long rope_positions, void* workspace, size_t workspace_bytes,
+                      void* stream);
+
+/*
  * Decode over one shard of a KV sequence (no counterpart in the reference, which has no
  * multi-GPU path; it generalises decode_kernel, dominus_ultra.py:288-413, by position
  * offsets). Key j of the shard rotates at kv_pos_offset + j, the query at q_pos. Writes fp32
@@ -144,8 +173,11 @@ int du_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, c
 int du_selftest_wait_timeout(int timeout_us, void* stream);
 
 /*
- * Read the device status words written when a bounded wait expires:
- * words[0] = error code (0 ok, DU_ERR_TIMEOUT), [1] wait site, [2..3] block index.
+ * Read the device status words (the first device-side error since the last reset):
+ *   words[0] = 0 ok;
+ *   DU_ERR_TIMEOUT: a bounded wait expired, [1] wait site, [2..3] block index;
+ *   DU_STATUS_BAD_SEQLEN: du_decode_kvcache met a cache length out of range, [1] sequence
+ *   index, [2] the length (as unsigned).
  * Synchronises the current device. reset != 0 clears them. Returns DU_OK or DU_ERR_CUDA.
  */
 int du_read_status(unsigned int* words4, int reset);

@@ -9,6 +9,7 @@ from .oracle import (  # noqa: F401
     apply_rope,
     apply_rope_backward,
     decode,
+    decode_kvcache,
     decode_partial,
     merge_partials,
     precompute_rope_cos_sin,

@@ -19,6 +19,11 @@ log-sum-exp the reference's evidence runner uses:
                                      ``past_len``, keys at ``0..past_len-1``, no mask
 * split-KV partial / merge ......... not in the reference; the LSE-weighted merge is the
                                      standard identity used by the build's multi-GPU decode.
+* KV-cache step (append + lengths) . not in the reference (its decode excludes the current
+                                     token, ``dominus_ultra.py:350``); restated as the reference
+                                     decode of each sequence over its own cache prefix
+                                     (``test_dominus.py:270-285`` with ``past_len = s_b``), after
+                                     writing the new key / value at row ``s_b``.
 
 Pinning: ``tests/test_oracle_golden.py`` checks this module against golden vectors produced by
 the reference itself (``tests/golden/make_golden.py``: the reference's own
@@ -44,6 +49,7 @@ __all__ = [
     "prefill_rows",
     "decode",
     "decode_partial",
+    "decode_kvcache",
     "merge_partials",
 ]
 
@@ -235,6 +241,48 @@ def decode(
     q_rot = apply_rope(q_new.cpu(), cos[L : L + 1], sin[L : L + 1])
     vf = v_cache.cpu().float().repeat_interleave(group, dim=1)
     return F.scaled_dot_product_attention(q_rot, k_rot, vf, is_causal=False)
+
+
+def decode_kvcache(
+    q_new: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    cos: torch.Tensor,
+    sin: torch.Tensor,
+    cache_seqlens: Sequence[int],
+    k_new: Optional[torch.Tensor] = None,
+    v_new: Optional[torch.Tensor] = None,
+    num_kv_heads: Optional[int] = None,
+) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """One generation step over a KV cache with per-sequence lengths, in fp32.
+
+    Sequence ``b`` holds ``s_b = cache_seqlens[b]`` tokens. With ``k_new`` / ``v_new``
+    (``[B,Hkv,1,D]``) they are first written to row ``s_b`` of copies of the caches and the
+    query attends to keys ``0..s_b``; otherwise to keys ``0..s_b-1``. The query rotates at
+    position ``s_b`` and key ``j`` at ``j``: the reference decode (``test_dominus.py:270-285``)
+    of each sequence over its own prefix, with the query position fixed at ``s_b``. A sequence
+    with no keys gives zeros. Returns ``(out fp32 [B,Hq,1,D], k_cache', v_cache')``.
+    """
+    B, Hq, _, D = q_new.shape
+    Hkv = num_kv_heads if num_kv_heads is not None else Hq
+    kc = k_cache.cpu().clone()
+    vc = v_cache.cpu().clone()
+    out = torch.zeros((B, Hq, 1, D), dtype=torch.float32)
+    for b in range(B):
+        s_b = int(cache_seqlens[b])
+        n = s_b
+        if k_new is not None:
+            kc[b, :, s_b] = k_new.cpu()[b, :, 0]
+            vc[b, :, s_b] = v_new.cpu()[b, :, 0]
+            n = s_b + 1
+        if n == 0:
+            continue
+        o, _ = decode_partial(
+            q_new[b : b + 1], kc[b : b + 1, :, :n], vc[b : b + 1, :, :n], cos, sin,
+            num_kv_heads=Hkv, q_pos=s_b, kv_pos_offset=0,
+        )
+        out[b, :, 0] = o[0]
+    return out, kc, vc
 
 
 def merge_partials(
