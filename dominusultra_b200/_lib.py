@@ -43,6 +43,14 @@ SIGNATURES = {
         [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _ll, _vp, _sz, _vp],
     ),
     "du_rope": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _ll, _ll, _i, _vp]),
+    "du_rope_segments": (
+        _i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _ll, _ll, _ll, _ll, _i, _vp]
+    ),
+    "du_prefill_block": (
+        _i,
+        [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i,
+         _ll, _ll, _ll, _i, _i, _f, _ll, _vp],
+    ),
     "du_decode_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
     "du_decode": (
         _i,

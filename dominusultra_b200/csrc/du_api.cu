@@ -216,6 +216,38 @@ size_t prefill_ws_bytes(int B, int Hkv, int T, int D) {
   return static_cast<size_t>(B) * Hkv * T * D * 2;
 }
 
+// The two-tile attention kernel over pre-rotated fp16 keys k_rot and values v of Tkv rows per
+// (b, kv head); query tiles cover rows [q_row0, q_row0 + Tq) of the T-row query tensor.
+template <int D, bool BF16, bool BLOCK>
+int launch_fa_t(const void* q, const void* k_rot, const void* v, du::PrefillParams prm, int B,
+                int Tkv, cudaStream_t st) {
+  using S = du::FaShape<D>;
+  const int dtype = BF16 ? DU_DTYPE_BF16 : DU_DTYPE_F16;
+  CUtensorMap tq, tk, tv;
+  int rc;
+  if ((rc = encode_map(&tq, q, dtype, D, prm.T, static_cast<long long>(B) * prm.Hq, S::SPAN / 2,
+                       S::BM, S::SPAN)) != DU_OK)
+    return rc;
+  if ((rc = encode_map(&tk, k_rot, DU_DTYPE_F16, D, Tkv, static_cast<long long>(B) * prm.Hkv,
+                       S::SPAN / 2, S::BN, S::SPAN)) != DU_OK)
+    return rc;
+  if ((rc = encode_map(&tv, v, dtype, D, Tkv, static_cast<long long>(B) * prm.Hkv, S::SPAN / 2,
+                       S::BN, S::SPAN)) != DU_OK)
+    return rc;
+  prm.n_qtiles = (prm.Tq + 2 * S::BM - 1) / (2 * S::BM);  // query-tile pairs
+  auto kern = du::prefill_fa_kernel<D, BF16, BLOCK>;
+  const int regs = launch_registers(kern);
+  if (regs * S::NTHREADS < 2 * 128 * S::REG_SOFTMAX + 128 * S::REG_OTHER)
+    return fail(DU_ERR_CUDA, "prefill kernel built with too few registers for its split");
+  cudaError_t e = ensure_smem_attr(kern, S::SMEM_BYTES);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(prefill)");
+  dim3 grid(static_cast<unsigned>(B * prm.Hq), static_cast<unsigned>(prm.n_qtiles));
+  kern<<<grid, S::NTHREADS, S::SMEM_BYTES, st>>>(tq, tk, tv, prm);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
+  return DU_OK;
+}
+
 template <int D, bool BF16>
 int launch_prefill_t(const void* q, const void* k, const void* v, du::PrefillParams prm, int B,
                      long long rope_positions, void* ws, cudaStream_t st) {
@@ -234,6 +266,8 @@ int launch_prefill_t(const void* q, const void* k, const void* v, du::PrefillPar
     rp.T = prm.T;
     rp.D = D;
     rp.pos_offset = 0;
+    rp.pos_split = prm.T;
+    rp.pos_offset1 = 0;
     if ((rc = launch_rope(rp, BF16, true, false, st)) != DU_OK) return rc;
     // 2) attention. Sequences up to 4096 (head_dim <= 64): one query tile per CTA, two CTAs per
     // SM, so one CTA's start-up and wind-down overlap the other's steady state (measured +3-5%
@@ -263,25 +297,7 @@ int launch_prefill_t(const void* q, const void* k, const void* v, du::PrefillPar
       if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
       return DU_OK;
     }
-    using S = du::FaShape<D>;
-    if ((rc = encode_map(&tq, q, dtype, D, prm.T, static_cast<long long>(B) * prm.Hq, S::SPAN / 2,
-                         S::BM, S::SPAN)) != DU_OK)
-      return rc;
-    if ((rc = encode_map(&tk, ws, DU_DTYPE_F16, D, prm.T, static_cast<long long>(B) * prm.Hkv,
-                         S::SPAN / 2, S::BN, S::SPAN)) != DU_OK)
-      return rc;
-    if ((rc = encode_map(&tv, v, dtype, D, prm.T, static_cast<long long>(B) * prm.Hkv,
-                         S::SPAN / 2, S::BN, S::SPAN)) != DU_OK)
-      return rc;
-    prm.n_qtiles = (prm.T + 2 * S::BM - 1) / (2 * S::BM);  // query-tile pairs
-    auto kern = du::prefill_fa_kernel<D, BF16>;
-    const int regs = launch_registers(kern);
-    if (regs * S::NTHREADS < 2 * 128 * S::REG_SOFTMAX + 128 * S::REG_OTHER)
-      return fail(DU_ERR_CUDA, "prefill kernel built with too few registers for its split");
-    e = ensure_smem_attr(kern, S::SMEM_BYTES);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(prefill)");
-    dim3 grid(static_cast<unsigned>(B * prm.Hq), static_cast<unsigned>(prm.n_qtiles));
-    kern<<<grid, S::NTHREADS, S::SMEM_BYTES, st>>>(tq, tk, tv, prm);
+    return launch_fa_t<D, BF16, false>(q, ws, v, prm, B, prm.T, st);
   } else {
     (void)rope_positions;
     (void)ws;
@@ -546,6 +562,85 @@ int decode_impl(const void* q, const void* kc, const void* vc, const void* cos, 
                       lse_f32, st);
 }
 
+// Rows [r0, r1) of a T-row tensor rotate at pos_offset + t below pos_split and
+// pos_offset1 + (t - pos_split) from it: every position they reach must be a table row.
+bool segments_covered(int T, long long split, long long off0, long long off1, long long r0,
+                      long long r1, long long rope_positions) {
+  (void)T;
+  if (r0 >= r1) return true;
+  if (r0 < split) {  // first segment: rows [r0, min(r1, split))
+    const long long hi = (r1 < split ? r1 : split) - 1;
+    if (off0 + r0 < 0 || off0 + hi >= rope_positions) return false;
+  }
+  if (r1 > split) {  // second segment: rows [max(r0, split), r1)
+    const long long lo = (r0 > split ? r0 : split) - split;
+    if (off1 + lo < 0 || off1 + (r1 - 1 - split) >= rope_positions) return false;
+  }
+  return true;
+}
+
+template <bool BF16>
+int launch_fa_d(const void* q, const void* k_rot, const void* v, const du::PrefillParams& prm,
+                int B, int Tkv, int D, cudaStream_t st) {
+  switch (D) {
+    case 16: return launch_fa_t<16, BF16, true>(q, k_rot, v, prm, B, Tkv, st);
+    case 32: return launch_fa_t<32, BF16, true>(q, k_rot, v, prm, B, Tkv, st);
+    case 64: return launch_fa_t<64, BF16, true>(q, k_rot, v, prm, B, Tkv, st);
+    case 128: return launch_fa_t<128, BF16, true>(q, k_rot, v, prm, B, Tkv, st);
+    default: return fail(DU_ERR_UNSUPPORTED, "block prefill supports head_dim 16, 32, 64, 128");
+  }
+}
+
+int prefill_block_impl(const void* q, const void* k_rot, const void* v, const void* cos,
+                       const void* sin, void* out, float* lse, float* acc_o, float* acc_lse,
+                       int acc_mode, int B, int Hq, int Hkv, int T, int Tkv, int q_row0, int Tq,
+                       int Tk, int causal, long long pos_split, long long pos_off0,
+                       long long pos_off1, int D, int dtype, float scale, long long rope_positions,
+                       cudaStream_t st) {
+  int rc = check_common(B, Hq, Hkv, T, D, dtype);
+  if (rc != DU_OK) return rc;
+  if (D > 128) return fail(DU_ERR_UNSUPPORTED, "block prefill supports head_dim 16, 32, 64, 128");
+  if (!q || !k_rot || !v || !cos || !sin || !out || !lse)
+    return fail(DU_ERR_INVALID, "null pointer argument");
+  if (!aligned16(q) || !aligned16(k_rot) || !aligned16(v) || !aligned16(cos) || !aligned16(sin) ||
+      !aligned16(out))
+    return fail(DU_ERR_INVALID, "q, k_rot, v, out and rope tables must be 16-byte aligned");
+  if (acc_mode < 0 || acc_mode > 2) return fail(DU_ERR_INVALID, "acc_mode must be 0, 1 or 2");
+  if (acc_mode != 0 && (!acc_o || !acc_lse || !aligned16(acc_o)))
+    return fail(DU_ERR_INVALID, "accumulators are required (acc_o 16-byte aligned) for acc_mode 1, 2");
+  if (Tkv <= 0 || Tk <= 0 || Tk > Tkv) return fail(DU_ERR_INVALID, "need 0 < Tk <= Tkv");
+  if (q_row0 < 0 || Tq <= 0 || static_cast<long long>(q_row0) + Tq > T)
+    return fail(DU_ERR_INVALID, "query rows [q_row0, q_row0 + Tq) must lie in [0, T)");
+  if (causal && (q_row0 != 0 || Tq != T || Tk != T))
+    return fail(DU_ERR_INVALID, "a causal block covers the whole query and key range (q_row0 = 0, Tq = Tk = T)");
+  if (pos_split < 0) return fail(DU_ERR_INVALID, "pos_split must be non-negative");
+  if (!segments_covered(T, pos_split, pos_off0, pos_off1, q_row0, static_cast<long long>(q_row0) + Tq,
+                        rope_positions))
+    return fail(DU_ERR_INVALID, "rope tables do not cover the query positions");
+  if (!(scale > 0.f)) return fail(DU_ERR_INVALID, "scale must be positive");
+  du::PrefillParams prm{};
+  prm.cos = cos;
+  prm.sin = sin;
+  prm.out = out;
+  prm.lse = lse;
+  prm.Hq = Hq;
+  prm.Hkv = Hkv;
+  prm.T = T;
+  prm.scale_log2 = scale * 1.4426950408889634f;
+  prm.q_row0 = q_row0;
+  prm.Tq = Tq;
+  prm.Tk = Tk;
+  prm.causal = causal ? 1 : 0;
+  prm.pos_split = pos_split;
+  prm.pos_off0 = pos_off0;
+  prm.pos_off1 = pos_off1;
+  prm.acc_o = acc_o;
+  prm.acc_lse = acc_lse;
+  prm.acc_mode = acc_mode;
+  return dtype == DU_DTYPE_BF16 ? launch_fa_d<true>(q, k_rot, v, prm, B, Tkv, D, st)
+                                : launch_fa_d<false>(q, k_rot, v, prm, B, Tkv, D, st);
+}
+
 // Workspace of du_decode_kvcache: chunk offsets [B + 1] (int64), {len, qpos} [B] (int2), then
 // the fragment-slot partials, o [(units + grid) * GT, D] and lse [(units + grid) * GT] fp32.
 struct KvcacheLayout {
@@ -697,6 +792,14 @@ int du_prefill(const void* q, const void* k, const void* v, const void* cos, con
   prm.T = T;
   prm.n_qtiles = (T + 127) / 128;
   prm.scale_log2 = scale * 1.4426950408889634f;
+  prm.q_row0 = 0;
+  prm.Tq = T;
+  prm.Tk = T;
+  prm.causal = 1;
+  prm.pos_split = T;
+  prm.pos_off0 = 0;
+  prm.pos_off1 = 0;
+  prm.acc_mode = 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool bf16 = dtype == DU_DTYPE_BF16;
   void* ws = workspace;
@@ -718,6 +821,14 @@ int du_prefill(const void* q, const void* k, const void* v, const void* cos, con
 int du_rope(const void* x, const void* cos, const void* sin, void* out, int B, int H, int T, int D,
             int dtype, int out_dtype, long long pos_offset, long long rope_positions, int backward,
             void* stream) {
+  return du_rope_segments(x, cos, sin, out, B, H, T, D, dtype, out_dtype, T, pos_offset, 0,
+                          rope_positions, backward, stream);
+}
+
+int du_rope_segments(const void* x, const void* cos, const void* sin, void* out, int B, int H,
+                     int T, int D, int dtype, int out_dtype, long long pos_split,
+                     long long pos_offset, long long pos_offset1, long long rope_positions,
+                     int backward, void* stream) {
   g_last_error.clear();
   if (B <= 0 || H <= 0 || T <= 0) return fail(DU_ERR_INVALID, "batch, heads, and sequence length must be positive");
   if (!valid_head_dim(D))
@@ -729,7 +840,8 @@ int du_rope(const void* x, const void* cos, const void* sin, void* out, int B, i
   if (!x || !cos || !sin || !out) return fail(DU_ERR_INVALID, "null pointer argument");
   if (!aligned16(x) || !aligned16(cos) || !aligned16(sin) || !aligned16(out))
     return fail(DU_ERR_INVALID, "all tensors must be 16-byte aligned");
-  if (pos_offset < 0 || pos_offset + T > rope_positions)
+  if (pos_split < 0 || pos_split > T) return fail(DU_ERR_INVALID, "pos_split must be in [0, T]");
+  if (!segments_covered(T, pos_split, pos_offset, pos_offset1, 0, T, rope_positions))
     return fail(DU_ERR_INVALID, "rope tables do not cover the positions");
   du::RopeParams rp{};
   rp.x = x;
@@ -740,6 +852,8 @@ int du_rope(const void* x, const void* cos, const void* sin, void* out, int B, i
   rp.T = T;
   rp.D = D;
   rp.pos_offset = pos_offset;
+  rp.pos_split = pos_split;
+  rp.pos_offset1 = pos_offset1;
   return launch_rope(rp, dtype == DU_DTYPE_BF16, out_dtype == DU_DTYPE_F16 && dtype != DU_DTYPE_F16,
                      backward != 0, static_cast<cudaStream_t>(stream));
 }
@@ -758,6 +872,18 @@ int du_decode(const void* q, const void* k_cache, const void* v_cache, const voi
   return decode_impl(q, k_cache, v_cache, cos, sin, out, nullptr, nullptr, B, Hq, Hkv, L, D,
                      dtype, scale, L, 0, rope_positions, workspace, workspace_bytes,
                      static_cast<cudaStream_t>(stream));
+}
+
+int du_prefill_block(const void* q, const void* k_rot, const void* v, const void* cos,
+                     const void* sin, void* out, float* lse, float* acc_o, float* acc_lse,
+                     int acc_mode, int B, int Hq, int Hkv, int T, int Tkv, int q_row0, int Tq,
+                     int Tk, int causal, long long pos_split, long long pos_off0,
+                     long long pos_off1, int D, int dtype, float scale, long long rope_positions,
+                     void* stream) {
+  g_last_error.clear();
+  return prefill_block_impl(q, k_rot, v, cos, sin, out, lse, acc_o, acc_lse, acc_mode, B, Hq, Hkv,
+                            T, Tkv, q_row0, Tq, Tk, causal, pos_split, pos_off0, pos_off1, D,
+                            dtype, scale, rope_positions, static_cast<cudaStream_t>(stream));
 }
 
 size_t du_decode_kvcache_workspace_size(int B, int Hq, int Hkv, int L, int D) {

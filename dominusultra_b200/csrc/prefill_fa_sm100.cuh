@@ -81,7 +81,10 @@ struct FaShape {
   static_assert(Q_BYTES % 1024 == 0 && KV_BYTES % 1024 == 0, "1024-byte alignment of swizzled tiles");
 };
 
-template <int D, bool BF16>
+// BLOCK: the block form of PrefillParams (query-row window, key range, causal or full, two-segment
+// positions, accumulate epilogue) for context-parallel prefill; the whole-sequence causal path
+// is the BLOCK = false instantiation, compiled without those generalisations.
+template <int D, bool BF16, bool BLOCK>
 __global__ void __launch_bounds__(384, 1)
     prefill_fa_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v, const PrefillParams p) {
@@ -106,9 +109,16 @@ __global__ void __launch_bounds__(384, 1)
   const int kvh = h / (p.Hq / p.Hkv);
   const int kv_row = b * p.Hkv + kvh;
   const int T = p.T;
-  const int q0a = pair * 2 * BM, q0b = q0a + BM;
-  const int nka = (q0a < T) ? (min(q0a + BM, T) - 1) / BN + 1 : 0;
-  const int nkb = (q0b < T) ? (min(q0b + BM, T) - 1) / BN + 1 : 0;
+  const int q_end = BLOCK ? p.q_row0 + p.Tq : T;  // query rows of this launch: [q_row0, q_end)
+  const int q0a = (BLOCK ? p.q_row0 : 0) + pair * 2 * BM, q0b = q0a + BM;
+  // KV tiles of a query tile: up to its diagonal (causal) or all Tk keys (block form, full).
+  auto tiles_of = [&](int q0x) {
+    if (q0x >= q_end) return 0;
+    if (BLOCK && !p.causal) return (p.Tk + BN - 1) / BN;
+    return (min(q0x + BM, q_end) - 1) / BN + 1;
+  };
+  const int nka = tiles_of(q0a);
+  const int nkb = tiles_of(q0b);
   const int nk_all = max(nka, nkb);
   auto q0 = [&](int x) { return x ? q0b : q0a; };
   auto n_kv = [&](int x) { return x ? nkb : nka; };
@@ -183,7 +193,14 @@ __global__ void __launch_bounds__(384, 1)
     const int x = warp >> 2;           // which query tile
     const int row = tid - 128 * x;     // row within the tile = TMEM lane
     const int qrow = q0(x) + row;
+    const bool row_ok = qrow < q_end;
     const int nk = n_kv(x);
+    // Keys past kmax are masked: the diagonal (causal) or the end of the keys (block form);
+    // tiles whose keys all lie at or below the tile's smallest kmax need no mask.
+    const int kmax = (!BLOCK || p.causal) ? qrow : p.Tk - 1;
+    const int kmax_tile = (!BLOCK || p.causal) ? q0(x) : p.Tk - 1;
+    const long long qpos = !BLOCK ? static_cast<long long>(qrow)
+                                  : ((qrow < p.pos_split) ? p.pos_off0 + qrow : p.pos_off1 + (qrow - p.pos_split));
     const uint32_t q_tile = sbase + (x ? S::OFF_QB : S::OFF_QA);
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t s_addr = tmem + lane_off + S::TM_S + x * BN;
@@ -199,15 +216,15 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll 1
       for (int c0 = 0; c0 < D / 16; c0 += NPQ) {
         uint4 cv[NPQ], sv[NPQ];
-        if (qrow < T)
-          load_rope_row<NPQ>(cv, sv, cosb + static_cast<size_t>(qrow) * D,
-                             sinb + static_cast<size_t>(qrow) * D, c0, 1);
+        if (row_ok)
+          load_rope_row<NPQ>(cv, sv, cosb + static_cast<size_t>(qpos) * D,
+                             sinb + static_cast<size_t>(qpos) * D, c0, 1);
         if (c0 == 0) {
           ok = mbar_wait(BAR_QF, 0, failed, 300);
           ok = __all_sync(0xffffffffu, ok);
         }
         if (!ok) break;
-        if (qrow < T) rotate_row<D, BF16, SPAN, NPQ>(q_tile, BM, row, c0, 1, cv, sv);
+        if (row_ok) rotate_row<D, BF16, SPAN, NPQ>(q_tile, BM, row, c0, 1, cv, sv);
       }
       if (ok) {
         fence_proxy_async_smem();
@@ -234,7 +251,7 @@ __global__ void __launch_bounds__(384, 1)
       // S in two halves: the first half is masked and reduced while the second half loads.
       float s[BN];
       const int k0 = j * BN;
-      const bool diag = k0 + BN - 1 > q0(x);  // tile crosses this query tile's diagonal
+      const bool diag = k0 + BN - 1 > kmax_tile;  // some key of the tile may be masked
 #pragma unroll
       for (int c = 0; c < BN / 2; c += 16) tmem_ld16(s_addr + c, s + c);
       tmem_wait_ld();
@@ -243,7 +260,7 @@ __global__ void __launch_bounds__(384, 1)
       if (diag) {
 #pragma unroll
         for (int c = 0; c < BN / 2; ++c)
-          if (k0 + c > qrow) s[c] = -INFINITY;
+          if (k0 + c > kmax) s[c] = -INFINITY;
       }
       float mq[4] = {fmaxf(s[0], s[1]), fmaxf(s[2], s[3]), fmaxf(s[4], s[5]), fmaxf(s[6], s[7])};
 #pragma unroll
@@ -259,7 +276,7 @@ __global__ void __launch_bounds__(384, 1)
       if (diag) {
 #pragma unroll
         for (int c = BN / 2; c < BN; ++c)
-          if (k0 + c > qrow) s[c] = -INFINITY;
+          if (k0 + c > kmax) s[c] = -INFINITY;
       }
 #pragma unroll
       for (int c = BN / 2; c < BN; c += 8) {
@@ -327,23 +344,59 @@ __global__ void __launch_bounds__(384, 1)
     }
     tc_fence_after();
     if (ok) {
-      const float inv_l = 1.0f / l;
-      const size_t orow = (static_cast<size_t>(bh) * T + qrow) * D;
+      const size_t ri = static_cast<size_t>(bh) * T + qrow;
+      const size_t orow = ri * D;
+      // Block weights: this block's normalised output and, with an accumulator, the running
+      // one, combined by their LSEs (log2 domain).
+      const float lse2 = m + lg2(l);
+      float w_blk = 1.0f / l, w_acc = 0.f, lse2_out = lse2;
+      if (BLOCK && p.acc_mode == 2 && row_ok) {
+        const float la2 = p.acc_lse[ri] * 1.4426950408889634f;
+        if (la2 > -INFINITY) {
+          const float mx = fmaxf(la2, lse2);
+          const float ea = ex2(la2 - mx), eb = ex2(lse2 - mx);
+          const float inv = 1.0f / (ea + eb);
+          w_acc = ea * inv;
+          w_blk = eb * inv / l;
+          lse2_out = mx + lg2(ea + eb);
+        }
+      }
 #pragma unroll
       for (int c = 0; c < D; c += 16) {
         float o[16];
         tmem_ld16(o_addr + c, o);
         tmem_wait_ld();
-        if (qrow < T) {
+        if (row_ok) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) o[i] *= w_blk;
+          if (BLOCK && p.acc_mode != 0) {
+            float4* acc = reinterpret_cast<float4*>(p.acc_o + orow + c);
+            if (w_acc > 0.f) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const float4 a = acc[i];
+                o[4 * i] = fmaf(a.x, w_acc, o[4 * i]);
+                o[4 * i + 1] = fmaf(a.y, w_acc, o[4 * i + 1]);
+                o[4 * i + 2] = fmaf(a.z, w_acc, o[4 * i + 2]);
+                o[4 * i + 3] = fmaf(a.w, w_acc, o[4 * i + 3]);
+              }
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+          }
           uint32_t w[8];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) w[i] = pack2<BF16>(o[2 * i] * inv_l, o[2 * i + 1] * inv_l);
+          for (int i = 0; i < 8; ++i) w[i] = pack2<BF16>(o[2 * i], o[2 * i + 1]);
           uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.out) + (orow + c) * 2);
           dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
           dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
         }
       }
-      if (qrow < T) p.lse[static_cast<size_t>(bh) * T + qrow] = (m + lg2(l)) * 0.69314718055994531f;
+      if (row_ok) {
+        const float lse_out = lse2_out * 0.69314718055994531f;
+        p.lse[ri] = lse_out;
+        if (BLOCK && p.acc_mode != 0) p.acc_lse[ri] = lse_out;
+      }
     }
   } else if (warp == 8) {
     // ------------------------------------------------------------------ TMA: Q, then the K ring

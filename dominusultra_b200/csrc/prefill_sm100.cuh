@@ -51,6 +51,25 @@ struct PrefillParams {
   int T;
   int n_qtiles;
   float scale_log2;  // softmax scale * log2(e)
+  // Block form (prefill_fa_kernel only; the causal whole-sequence call sets q_row0 = 0,
+  // Tq = Tk = T, causal = 1, pos_split = T, pos_off0 = 0, acc_mode = 0):
+  //   query rows [q_row0, q_row0 + Tq) of the T-row tensors, keys [0, Tk) of the KV tensors;
+  //   causal: key t visible to query row t' iff t <= t' (local rows; needs q_row0 = 0,
+  //   Tq = Tk = T); otherwise every key is visible;
+  //   query row t rotates at pos_off0 + t for t < pos_split, pos_off1 + (t - pos_split) beyond;
+  //   acc_mode 1: the block's (out, lse) also overwrite the fp32 accumulators acc_o [B, Hq, T, D]
+  //   and acc_lse [B, Hq, T]; 2: they are LSE-merged into them. In both, out and lse receive the
+  //   merged result.
+  int q_row0;
+  int Tq;
+  int Tk;
+  int causal;
+  long long pos_split;
+  long long pos_off0;
+  long long pos_off1;
+  float* acc_o;
+  float* acc_lse;
+  int acc_mode;
 };
 
 template <int D>

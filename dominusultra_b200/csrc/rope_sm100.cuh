@@ -4,7 +4,9 @@
 //   forward  (i < D/2): y_i = x_i c_i - x_{i+D/2} s_i,   y_{i+D/2} = x_{i+D/2} c_i + x_i s_i
 //   backward (the transpose): y_i = x_i c_i + x_{i+D/2} s_i, y_{i+D/2} = x_{i+D/2} c_i - x_i s_i
 //
-// with c_i = cos[pos, i], s_i = sin[pos, i] and pos = t + pos_offset for row t of [B, H, T, D].
+// with c_i = cos[pos, i], s_i = sin[pos, i] and, for row t of [B, H, T, D], pos = pos_offset + t
+// for t < pos_split and pos_offset1 + (t - pos_split) beyond (two position segments: a rank of a
+// context-parallel prefill holds two non-adjacent chunks of the sequence along T).
 // The rotation runs in fp32 on 16-bit inputs and rounds once on output (the reference rounds
 // the same products through its input dtype). The output is the input dtype, or fp16 for the
 // attention operand path (rotated K feeding the fp16 tensor-core QK^T).
@@ -27,6 +29,8 @@ struct RopeParams {
   int T;
   int D;
   long long pos_offset;
+  long long pos_split;    // rows t >= pos_split use the second segment (T: one segment)
+  long long pos_offset1;
 };
 
 template <bool BF16, bool OUT_F16, bool BACKWARD>
@@ -43,7 +47,8 @@ __global__ void __launch_bounds__(256) rope_kernel(const RopeParams p) {
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
     const long long row = i / cpr;
     const int c = static_cast<int>(i - row * cpr);
-    const long long pos = row % p.T + p.pos_offset;
+    const long long t = row % p.T;
+    const long long pos = (t < p.pos_split) ? p.pos_offset + t : p.pos_offset1 + (t - p.pos_split);
     const uint8_t* xr = xb + row * row_bytes;
     const uint4 lo = ldg_stream_v4(xr + c * 16);
     const uint4 hi = ldg_stream_v4(xr + tab_bytes + c * 16);

@@ -73,6 +73,41 @@ int du_rope(const void* x, const void* cos, const void* sin, void* out, int B, i
             void* stream);
 
 /*
+ * du_rope with two position segments: row t of [B, H, T, D] rotates at pos_offset + t for
+ * t < pos_split and at pos_offset1 + (t - pos_split) from pos_split on (0 <= pos_split <= T).
+ * A rank of a context-parallel prefill holds two non-adjacent chunks of the sequence along T
+ * (zigzag sharding) and rotates its keys once with this. du_rope(..., pos_offset, ...) equals
+ * du_rope_segments(..., pos_split = T, pos_offset, 0, ...).
+ */
+int du_rope_segments(const void* x, const void* cos, const void* sin, void* out, int B, int H,
+                     int T, int D, int dtype, int out_dtype, long long pos_split,
+                     long long pos_offset, long long pos_offset1, long long rope_positions,
+                     int backward, void* stream);
+
+/*
+ * One block of a context-parallel (ring) prefill (no counterpart in the reference, which is
+ * single-GPU; it generalises prefill_kernel, dominus_ultra.py:119-285, to a query range against
+ * a key range). head_dim 16..128.
+ *   q [B, Hq, T, D] (input dtype, rotated here), k_rot [B, Hkv, Tkv, D] fp16 keys already
+ *   rotated at their absolute positions (du_rope_segments, out_dtype DU_DTYPE_F16),
+ *   v [B, Hkv, Tkv, D] (input dtype).
+ *   Query rows [q_row0, q_row0 + Tq) attend to keys [0, Tk). causal != 0: key t is visible to
+ *   query row t' iff t <= t' (then q_row0 = 0 and Tq = Tk = T); causal == 0: every key is
+ *   visible. Query row t rotates at pos_off0 + t (t < pos_split) or pos_off1 + (t - pos_split).
+ *   out [B, Hq, T, D] and lse [B, Hq, T] (natural log) are written for the block's rows only.
+ *   acc_mode 0: out / lse are this block's attention. acc_mode 1: they also overwrite the fp32
+ *   accumulators acc_o [B, Hq, T, D] / acc_lse [B, Hq, T]. acc_mode 2: the block is LSE-merged
+ *   into the accumulators (a row with acc_lse = -inf takes the block alone) and out / lse
+ *   receive the merged result, so after a row's last block out / lse are final.
+ */
+int du_prefill_block(const void* q, const void* k_rot, const void* v, const void* cos,
+                     const void* sin, void* out, float* lse, float* acc_o, float* acc_lse,
+                     int acc_mode, int B, int Hq, int Hkv, int T, int Tkv, int q_row0, int Tq,
+                     int Tk, int causal, long long pos_split, long long pos_off0,
+                     long long pos_off1, int D, int dtype, float scale, long long rope_positions,
+                     void* stream);
+
+/*
  * Workspace bytes du_decode / du_decode_partial need for these sizes on the current device
  * (0 when every row's cache is handled by one CTA).
  */

@@ -14,5 +14,6 @@ from .oracle import (  # noqa: F401
     merge_partials,
     precompute_rope_cos_sin,
     prefill,
+    prefill_block,
     prefill_rows,
 )

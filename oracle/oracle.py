@@ -19,6 +19,8 @@ log-sum-exp the reference's evidence runner uses:
                                      ``past_len``, keys at ``0..past_len-1``, no mask
 * split-KV partial / merge ......... not in the reference; the LSE-weighted merge is the
                                      standard identity used by the build's multi-GPU decode.
+* context-parallel block ........... not in the reference: ``prefill`` restricted to a query row
+                                     range at given positions against a key range (ring prefill).
 * KV-cache step (append + lengths) . not in the reference (its decode excludes the current
                                      token, ``dominus_ultra.py:350``); restated as the reference
                                      decode of each sequence over its own cache prefix
@@ -47,6 +49,7 @@ __all__ = [
     "apply_rope",
     "prefill",
     "prefill_rows",
+    "prefill_block",
     "decode",
     "decode_partial",
     "decode_kvcache",
@@ -144,6 +147,51 @@ def prefill(
         )[0, 0]
         scores = (qr @ kr.transpose(0, 1)) * scale
         lse[b, h] = torch.logsumexp(scores.masked_fill(mask, float("-inf")), dim=-1)
+    return out, lse
+
+
+def prefill_block(
+    q: torch.Tensor,
+    k_rot: torch.Tensor,
+    v: torch.Tensor,
+    cos: torch.Tensor,
+    sin: torch.Tensor,
+    q_row0: int,
+    tq: int,
+    tk: int,
+    causal: bool,
+    pos_split: int,
+    pos_off0: int,
+    pos_off1: int,
+    num_kv_heads: Optional[int] = None,
+) -> Tuple[torch.Tensor, torch.Tensor]:
+    """One block of a context-parallel prefill in fp32: ``(out [B,Hq,tq,D], lse [B,Hq,tq])``.
+
+    Not in the reference (single-GPU); the same mathematics as ``prefill`` restricted to query
+    rows ``[q_row0, q_row0 + tq)`` of ``q`` — row ``t`` rotated at ``pos_off0 + t`` below
+    ``pos_split`` and ``pos_off1 + (t - pos_split)`` from it — against keys ``[0, tk)`` of
+    ``k_rot`` (already rotated at their positions) and ``v``. ``causal``: key ``j`` visible to
+    row ``t`` iff ``j <= t``; otherwise all keys are visible.
+    """
+    B, Hq, T, D = q.shape
+    Hkv = num_kv_heads if num_kv_heads is not None else Hq
+    scale = 1.0 / math.sqrt(D)
+    rows = torch.arange(q_row0, q_row0 + tq)
+    pos = torch.where(rows < pos_split, pos_off0 + rows, pos_off1 + (rows - pos_split))
+    qr = apply_rope(q[:, :, q_row0 : q_row0 + tq].cpu(), cos[pos], sin[pos])
+    kr = k_rot[:, :, :tk].cpu().float()
+    vf = v[:, :, :tk].cpu().float()
+    out = torch.empty((B, Hq, tq, D), dtype=torch.float32)
+    lse = torch.empty((B, Hq, tq), dtype=torch.float32)
+    mask = (torch.arange(tk)[None, :] > rows[:, None]) if causal else None
+    for h in range(Hq):
+        kvh = _kv_head(h, Hq, Hkv)
+        sc = torch.einsum("btd,bjd->btj", qr[:, h], kr[:, kvh]) * scale
+        if mask is not None:
+            sc = sc.masked_fill(mask, float("-inf"))
+        l = torch.logsumexp(sc, dim=-1)
+        out[:, h] = torch.einsum("btj,bjd->btd", torch.exp(sc - l[..., None]), vf[:, kvh])
+        lse[:, h] = l
     return out, lse
 
 
