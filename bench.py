@@ -46,9 +46,9 @@ DECODE = dict(B=8, H=32, Hkv=32, L=2048, D=64, base=10000.0)
 DECODE_LONG = dict(B=4, H=32, Hkv=8, L=131072, D=128, base=500000.0)
 
 # Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum, bytes) of the dominant
-# kernel from the ncu captures summarised under profiles/ (prefill: prefill_fa_kernel at the
+# kernel from the ncu captures summarised under profiles/ (prefill: prefill_fa1_kernel at the
 # bench shape; decode: decode_kernel at the bench shape).
-NCU_TRAFFIC = {"prefill": 50655232 + 13824, "decode": 134578176 + 4145920}
+NCU_TRAFFIC = {"prefill": 50646784 + 14848, "decode": 134578176 + 4145920}
 
 
 def prefill_flops(B, H, S, D):
@@ -583,7 +583,7 @@ def main():
                 "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                 "frac": achieved / peak, "traffic": NCU_TRAFFIC["prefill"],
                 "peak_kind": f"{peak_kind} bf16 dense (burst)",
-                "kernel": "prefill_fa_kernel", "kernel_ms": attn_ms,
+                "kernel": "prefill_fa1_kernel", "kernel_ms": attn_ms,
                 "algorithmic_flops": flops,
                 "rope_pass": {"kernel": "rope_kernel (keys, bf16 -> fp16)", "ms": rope_ms,
                               "gbs": rope_bytes(cfg) / (rope_ms / 1000.0) / 1e9},
