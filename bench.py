@@ -461,6 +461,48 @@ def reference_gpu_baseline(device, steps, warmup):
         return {"unavailable": f"{type(e).__name__}: {str(e).splitlines()[0][:200]}"}
 
 
+RING = dict(B=4, H=32, Hkv=8, S=32768, D=128, base=500000.0)
+
+
+def bench_ring(dist, rank, world, device, stream, steps, warmup, peaks, peak_kind, seq):
+    """Context-parallel prefill of the Llama-3-8B-shaped layer: the sequence zigzag-sharded over
+    the ranks (chunks r and 2N-1-r), K/V passed around the ring with NCCL point-to-point,
+    overlapped with the block kernels. Strong scaling: the whole sequence is fixed."""
+    from dominusultra_b200 import precompute_rope_cos_sin, ring
+
+    c = dict(RING, S=seq or RING["S"])
+    B, H, Hkv, S, D = c["B"], c["H"], c["Hkv"], c["S"], c["D"]
+    tc = S // (2 * world)
+    g = torch.Generator(device=device).manual_seed(5000 + rank)
+    q = torch.randn(B, H, 2 * tc, D, generator=g, device=device).to(torch.bfloat16)
+    k = torch.randn(B, Hkv, 2 * tc, D, generator=g, device=device).to(torch.bfloat16)
+    v = torch.randn(B, Hkv, 2 * tc, D, generator=g, device=device).to(torch.bfloat16)
+    cos, sin = precompute_rope_cos_sin(S, D, device, torch.bfloat16, c["base"])
+
+    def step(_i):
+        ring.ring_prefill(q, k, v, cos, sin, Hkv)
+
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    barrier(dist)
+    ms = time_region(step, steps, stream) / steps
+    ms = max_over_ranks(dist, ms, device)
+    flops = prefill_flops(B, H, S, D)
+    tflops = flops / (ms / 1000.0) / 1e12
+    return {
+        "metric": "context-parallel causal prefill TFLOP/s (whole job)", "value": tflops,
+        "unit": "TFLOP/s", "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "dtype": "bf16",
+        "data": "synthetic N(0,1) bf16, seeded per rank",
+        "config": {"workload": f"prefill B{B} H{H} Hkv{Hkv} S{S} D{D} causal RoPE base 5e5, "
+                               f"sequence zigzag-sharded over {world} GPU(s), ring of NCCL "
+                               "point-to-point K/V transfers"},
+        "per_gpu_frac_of_peak": tflops / world / peaks["bf16_tflops_sustained"],
+        "peak_kind": f"{peak_kind} bf16 dense (sustained)",
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -471,6 +513,9 @@ def main():
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-long-decode", action="store_true")
     ap.add_argument("--no-reference-gpu", action="store_true")
+    ap.add_argument("--ring", action="store_true",
+                    help="only the context-parallel (ring) prefill of the Llama-3-8B-shaped layer")
+    ap.add_argument("--ring-seq", type=int, default=0, help="sequence length of --ring")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -485,6 +530,14 @@ def main():
     stream = torch.cuda.current_stream(device)
     peaks, peak_kind = load_peaks()
     _lib.load()
+    if args.ring:
+        line = bench_ring(dist, rank, world, device, stream, args.steps, args.warmup, peaks,
+                          peak_kind, args.ring_seq)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        if dist is not None:
+            dist.destroy_process_group()
+        return 0
 
     cfg = PREFILL
     B, H, Hkv, S, D = cfg["B"], cfg["H"], cfg["Hkv"], cfg["S"], cfg["D"]
