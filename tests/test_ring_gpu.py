@@ -138,6 +138,48 @@ def test_ring_emulated_on_one_gpu(cuda_device, world, tc, D, Hq, Hkv):
     assert_no_device_timeouts()
 
 
+def test_ring_emulated_eight_ranks_long_context_sampled_rows(cuda_device):
+    """The eight-rank ring of the Llama-3-8B-shaped layer's length (S = 32768, D128, base 5e5,
+    four query heads on one KV head), emulated on one GPU, checked on sampled rows of the
+    assembled output (each an exact oracle comparison: causal row i depends only on keys <= i)."""
+    world, B, Hq, Hkv, S, D = 8, 1, 4, 1, 32768, 128
+    tc = S // (2 * world)
+    dtype = torch.bfloat16
+    q = randn((B, Hq, S, D), 600, dtype)
+    k = randn((B, Hkv, S, D), 601, dtype)
+    v = randn((B, Hkv, S, D), 602, dtype)
+    cos, sin = precompute_rope_cos_sin(S, D, "cpu", dtype, 500000.0)
+    cd, sd = cos.cuda(), sin.cuda()
+    qs = [ring.zigzag_shard(q, r, world).cuda() for r in range(world)]
+    ks = [ring.rotate_keys(ring.zigzag_shard(k, r, world).cuda(), cd, sd, r, world)
+          for r in range(world)]
+    vs = [ring.zigzag_shard(v, r, world).cuda() for r in range(world)]
+    outs, lses = [], []
+    acc_o = torch.empty((B, Hq, 2 * tc, D), device="cuda")
+    acc_lse = torch.empty((B, Hq, 2 * tc), device="cuda")
+    for r in range(world):
+        out = torch.empty_like(qs[r])
+        lse = torch.empty((B, Hq, 2 * tc), device="cuda")
+        pos = ring.zigzag_positions(r, world, tc)
+        for blk in ring.ring_schedule(r, world, tc):
+            ring.prefill_block(qs[r], ks[blk.src], vs[blk.src], cd, sd, out, lse, acc_o, acc_lse,
+                               blk, pos, Hkv)
+        outs.append(out.cpu())
+        lses.append(lse.cpu())
+    torch.cuda.synchronize()
+    out, lse = ring.zigzag_unshard(outs), ring.zigzag_unshard(lses)
+    g = torch.Generator().manual_seed(603)
+    # rows at every chunk boundary of the zigzag layout, plus random ones
+    edges = [c * tc + d for c in range(2 * world) for d in (0, tc - 1)]
+    rows = sorted(set(edges + torch.randint(0, S, (192,), generator=g).tolist()))
+    for h in (0, 3):
+        ro, rl = oracle.prefill_rows(q, k, v, cos, sin, Hkv, 0, h, rows)
+        assert max_abs(out[0, h, rows], ro) <= OUT_TOL
+        assert max_abs(lse[0, h, rows], rl) <= LSE_TOL
+    assert torch.isfinite(out.float()).all()
+    assert_no_device_timeouts()
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
