@@ -375,11 +375,19 @@ DecodePlan plan_decode(int B, int Hq, int Hkv, int L, int D) {
   pl.total_chunks = units * pl.cpu;
   const long long grid = pl.total_chunks < ctas ? pl.total_chunks : ctas;
   const long long per = pl.total_chunks / grid;  // chunks per CTA, at least
-  // Whole units when they spread evenly, are plentiful, or are too short to be worth cutting
-  // (fragments of fewer than four chunks would cost more in partials than they balance).
-  if (units % ctas == 0 || units >= 8 * ctas || per < 4) {
+  // Whole units (no partials, no merge) when they spread evenly, are plentiful, are too short to
+  // be worth cutting (fragments of fewer than four chunks cost more in partials than they
+  // balance), or — for the one- and two-head kernels, several CTAs per SM — when they keep at
+  // least three quarters of the SMs streaming. Measured on B200, one-head units: 128 / 192 / 256
+  // units 3 / 7 / 28 % faster whole than split; the four-head kernel (one CTA per SM) split is
+  // faster at 128 and 320 units (3 / 21 %). Beyond the resident CTAs each CTA takes k units,
+  // k = ceil(units / ctas), over ceil(units / k) CTAs (512 units: 31.2 -> 27.0 us).
+  const bool whole = units % ctas == 0 || units >= 8 * ctas || per < 4 ||
+                     (pl.GT <= 2 && 4 * units >= 3LL * sm_count());
+  if (whole) {
     pl.n_split = 1;
-    pl.grid = static_cast<int>(units < ctas ? units : ctas);
+    const long long k = (units + ctas - 1) / ctas;  // units per CTA
+    pl.grid = static_cast<int>((units + k - 1) / k);
     return pl;
   }
   long long slots = (pl.cpu - 1 + per - 1) / per + 1;  // CTAs one unit's chunks can span
