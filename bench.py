@@ -48,7 +48,7 @@ DECODE_LONG = dict(B=4, H=32, Hkv=8, L=131072, D=128, base=500000.0)
 # Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum, bytes) of the dominant
 # kernel from the ncu captures summarised under profiles/ (prefill: prefill_fa1_kernel at the
 # bench shape; decode: decode_kernel at the bench shape).
-NCU_TRAFFIC = {"prefill": 50646784 + 14848, "decode": 134578176 + 4145920}
+NCU_TRAFFIC = {"prefill": 50646784 + 14848, "decode": 134576128 + 5068032}
 
 
 def prefill_flops(B, H, S, D):
