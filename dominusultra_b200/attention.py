@@ -115,8 +115,28 @@ def _aligned(t: torch.Tensor) -> torch.Tensor:
     return t if t.data_ptr() % 16 == 0 else t.clone()
 
 
+_RAW_STREAM = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream(device: torch.device) -> int:
+    """Handle of torch's current stream on `device` (without building a Stream object when the
+    raw getter is available: this is on every call's host path)."""
+    if _RAW_STREAM is not None:
+        return _RAW_STREAM(device.index if device.index is not None else torch.cuda.current_device())
     return torch.cuda.current_stream(device).cuda_stream
+
+
+# Workspace sizes by (entry point, sizes, device): a ctypes call per launch otherwise.
+_WS_SIZES = {}
+
+
+def _ws_size(fn_name: str, B: int, Hq: int, Hkv: int, L: int, D: int, device) -> int:
+    key = (fn_name, B, Hq, Hkv, L, D, device.index)
+    n = _WS_SIZES.get(key)
+    if n is None:
+        n = int(getattr(_lib.load(), fn_name)(B, Hq, Hkv, L, D))
+        _WS_SIZES[key] = n
+    return n
 
 
 def _ptr(t: Optional[torch.Tensor]) -> int:
@@ -205,7 +225,8 @@ def dominus_ultra_prefill(
     with _OnDevice(q.device):
         stream = _stream(q.device)
         ws, ws_bytes = _cached_workspace(
-            "prefill", int(lib.du_prefill_workspace_size(B, Hq, KvH, T, D)), q.device, stream
+            "prefill", _ws_size("du_prefill_workspace_size", B, Hq, KvH, T, D, q.device), q.device,
+            stream,
         )
         rc = lib.du_prefill(
             _ptr(q), _ptr(k), _ptr(v), _ptr(cos), _ptr(sin), _ptr(out), _ptr(lse),
@@ -230,7 +251,7 @@ def _cached_workspace(kind: str, nbytes: int, device, stream: int):
 
 
 def _workspace(B: int, Hq: int, Hkv: int, L: int, D: int, device, stream: int):
-    nbytes = int(_lib.load().du_decode_workspace_size(B, Hq, Hkv, L, D))
+    nbytes = _ws_size("du_decode_workspace_size", B, Hq, Hkv, L, D, device)
     return _cached_workspace("decode", nbytes, device, stream)
 
 
@@ -398,7 +419,7 @@ def dominus_ultra_decode_kvcache(
         stream = _stream(q_new.device)
         ws, nbytes = _cached_workspace(
             "decode_kvcache",
-            int(lib.du_decode_kvcache_workspace_size(B, Hq, KvH, max_len, D)),
+            _ws_size("du_decode_kvcache_workspace_size", B, Hq, KvH, max_len, D, q_new.device),
             q_new.device,
             stream,
         )

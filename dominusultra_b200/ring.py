@@ -172,8 +172,11 @@ def ring_prefill(
     """
     import torch.distributed as dist
 
-    world = dist.get_world_size(group)
-    rank = dist.get_rank(group)
+    if dist.is_available() and dist.is_initialized():
+        world = dist.get_world_size(group)
+        rank = dist.get_rank(group)
+    else:  # no process group: a ring of one rank (the causal prefill of the local sequence)
+        world, rank = 1, 0
     if q.ndim != 4 or k.ndim != 4 or v.ndim != 4:
         raise ValueError("q, k, and v must be rank-4 tensors")
     B, Hq, T2, D = q.shape
