@@ -592,7 +592,51 @@ def main():
         e2e_step(i)
     torch.cuda.synchronize()
     barrier(dist)
-    e2e_ms = time_region(e2e_step, args.steps, stream) / args.steps
+    e2e_serial_ms = time_region(e2e_step, args.steps, stream) / args.steps
+    e2e_serial_ms = max_over_ranks(dist, e2e_serial_ms, device)
+
+    # The same steps with the copies on their own streams, double-buffered: step i+1's inputs
+    # cross PCIe while step i computes and step i-1's outputs come back (host-to-device and
+    # device-to-host copies run on separate copy engines). Every step still copies its own
+    # inputs in and its own outputs out inside the timed region.
+    h2d_st, d2h_st = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    dev_in = [tuple(torch.empty(t.shape, dtype=t.dtype, device=device) for t in host_sets[0])
+              for _ in range(2)]
+    h2d_done = [torch.cuda.Event() for _ in range(2)]
+    comp_done = [torch.cuda.Event() for _ in range(2)]
+
+    def e2e_pipelined(n):
+        first = torch.cuda.Event(enable_timing=True)
+        last = torch.cuda.Event(enable_timing=True)
+        first.record(stream)
+        h2d_st.wait_event(first)
+        d2h_st.wait_event(first)
+        for i in range(n):
+            slot = i % 2
+            with torch.cuda.stream(h2d_st):
+                if i >= 2:
+                    h2d_st.wait_event(comp_done[slot])  # step i-2 has finished reading the slot
+                for dst, src in zip(dev_in[slot], host_sets[i % 2]):
+                    dst.copy_(src, non_blocking=True)
+                h2d_done[slot].record(h2d_st)
+            stream.wait_event(h2d_done[slot])
+            q, k, v = dev_in[slot]
+            out, lse = dominus_ultra_prefill(q, k, v, cos, sin, Hkv)
+            comp_done[slot].record(stream)
+            with torch.cuda.stream(d2h_st):
+                d2h_st.wait_event(comp_done[slot])
+                out_h.copy_(out, non_blocking=True)
+                lse_h.copy_(lse, non_blocking=True)
+            out.record_stream(d2h_st)
+            lse.record_stream(d2h_st)
+        last.record(d2h_st)
+        last.synchronize()
+        return first.elapsed_time(last)
+
+    e2e_pipelined(2)
+    torch.cuda.synchronize()
+    barrier(dist)
+    e2e_ms = e2e_pipelined(args.steps) / args.steps
     e2e_ms = max_over_ranks(dist, e2e_ms, device)
     h2d = sum(t.numel() * t.element_size() for t in host_sets[0])
     d2h = out_h.numel() * out_h.element_size() + lse_h.numel() * 4
@@ -642,7 +686,10 @@ def main():
                               "gbs": rope_bytes(cfg) / (rope_ms / 1000.0) / 1e9},
             },
             "e2e": {"value": world * flops / (e2e_ms / 1000.0) / 1e12, "unit": "TFLOP/s",
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+                    "copies": "pinned host buffers; H2D and D2H on their own streams, double-buffered "
+                              "across steps",
+                    "serial_ms_per_step": e2e_serial_ms},
             "gpu_launches": 2 * args.steps,  # per step: key rotation + attention
             "clocks": clocks,
             "device_status": status,
