@@ -63,6 +63,7 @@ struct DecodeParams {
   // so every fragment has its own slot).
   const long long* pre;
   const int2* lenq;
+  const int* vl_whole;  // set by the prep kernel: whole units round-robin, final rows to out
   int B;
   int ub;  // units per sequence: Hkv * n_gchunk
   int varlen;
@@ -89,6 +90,7 @@ struct DecodeWalk {
   long long cur, hi;
   long long per;  // per-sequence lengths: chunks per CTA
   int b;          // per-sequence lengths: the sequence holding chunk `cur`
+  bool whole;     // per-sequence lengths: whole units round-robin (no partials)
   // Chunks per CTA of the per-sequence-length walk; decode_merge_varlen_kernel uses the same.
   __device__ __forceinline__ static long long varlen_per(long long total, long long grid) {
     const long long per = (total + grid - 1) / grid;
@@ -96,6 +98,12 @@ struct DecodeWalk {
   }
   __device__ __forceinline__ void init(const DecodeParams& p) {
     if (p.varlen) {
+      whole = *p.vl_whole != 0;
+      if (whole) {
+        cur = blockIdx.x;
+        hi = p.n_units;
+        return;
+      }
       // Equal ranges of the flattened chunks that are actually present (pre[B] of them).
       const long long total = p.pre[p.B];
       per = varlen_per(total, gridDim.x);
@@ -127,6 +135,17 @@ struct DecodeWalk {
   }
   __device__ __forceinline__ bool next(const DecodeParams& p, int CK, DecodeFrag& f) {
     if (cur >= hi) return false;
+    if (p.varlen && whole) {
+      const int2 lq = p.lenq[cur / p.ub];
+      f.unit = static_cast<int>(cur);
+      f.kbeg = 0;
+      f.kend = lq.x;
+      f.slot = -1;  // final rows, written to out
+      f.last = true;
+      f.qpos = lq.y;
+      cur += gridDim.x;
+      return true;
+    }
     if (p.varlen) {
       while (p.pre[b + 1] <= cur) ++b;  // every sequence has at least one chunk per unit
       const long long base = p.pre[b];
@@ -602,11 +621,11 @@ __global__ void __launch_bounds__(DecodeShape<D, GT>::NTHREADS, (GT == 1) ? 3 : 
       }
       const size_t row = static_cast<size_t>(b) * p.Hq + h0 + gg;
       const float val = (Lsum > 0.f) ? A / Lsum : 0.f;
-      if (p.varlen) {
+      if (p.varlen && split >= 0) {
         const size_t fs = static_cast<size_t>(split) * GT + gg;  // fragment slot row
         p.o_part[fs * D + d] = val;
         if (d == 0) p.lse_part[fs] = (Lsum > 0.f) ? (M + lg2(Lsum)) * 0.69314718055994531f : -INFINITY;
-      } else if (p.mode == 0) {
+      } else if (p.mode == 0 || split < 0) {
         if constexpr (BF16) {
           static_cast<__nv_bfloat16*>(p.out)[row * D + d] = __float2bfloat16_rn(val);
         } else {
@@ -722,7 +741,10 @@ struct DecodePrepParams {
   void* v_cache;
   long long* pre;      // out [B + 1]: flattened chunk offsets (DecodeParams::pre)
   int2* lenq;          // out [B]: {keys attended, query position}
+  int* vl_whole;       // out: 1 = the split kernel takes whole units round-robin
   int B, Hkv, L, D, CK, ub, append;
+  int whole_ok;        // the unit count allows whole units (decided on the host)
+  int grid;            // CTAs of the split kernel
   long long rope_positions;
 };
 
@@ -771,6 +793,36 @@ __global__ void __launch_bounds__(256) decode_prep_kernel(const DecodePrepParams
       __syncthreads();
     }
     if (tid == 0) p.pre[0] = 0;
+    // Whole units round-robin (no partials, no merge) when their load is even: the busiest CTA
+    // carries at most 5/4 of the average over the CTAs that get a unit (lengths near uniform);
+    // otherwise the length-balanced split walk.
+    __syncthreads();
+    int whole = 0;
+    if (p.whole_ok) {
+      const long long units = static_cast<long long>(p.B) * p.ub;
+      long long mk = 0;
+      for (int c = tid; c < p.grid; c += blockDim.x) {
+        long long sum = 0;
+        for (long long u = c; u < units; u += p.grid) {
+          const int nch = (p.lenq[u / p.ub].x + p.CK - 1) / p.CK;
+          sum += nch > 1 ? nch : 1;
+        }
+        mk = sum > mk ? sum : mk;
+      }
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) {
+        const long long y = __shfl_xor_sync(0xffffffffu, mk, o);
+        mk = y > mk ? y : mk;
+      }
+      if (lane == 0) warp_tot[warp] = mk;
+      __syncthreads();
+      if (tid == 0) {
+        for (int w2 = 0; w2 < 8; ++w2) mk = warp_tot[w2] > mk ? warp_tot[w2] : mk;
+        const long long active = units < p.grid ? units : p.grid;
+        whole = (4 * mk * active <= 5 * p.pre[p.B]) ? 1 : 0;
+      }
+    }
+    if (tid == 0) *p.vl_whole = whole;
   }
   if (p.append) {
     const int cpr = p.D / 8;  // 16-byte pieces per row
@@ -793,10 +845,11 @@ __global__ void __launch_bounds__(256) decode_prep_kernel(const DecodePrepParams
 // DecodeWalk); fragment (u, c) wrote row (u + c) * GT + gg.
 __global__ void __launch_bounds__(128) decode_merge_varlen_kernel(
     const float* __restrict__ o_parts, const float* __restrict__ lse_parts,
-    const long long* __restrict__ pre, int Hq, int Hkv, int GT, int ub, int B, int D,
-    int split_grid, void* out, int out_kind) {
+    const long long* __restrict__ pre, const int* __restrict__ vl_whole, int Hq, int Hkv, int GT,
+    int ub, int B, int D, int split_grid, void* out, int out_kind) {
   __shared__ float w[MERGE_MAX_R];
   griddep_wait();  // the split kernel has completed
+  if (*vl_whole) return;  // whole units: the split kernel wrote the final rows
   const long long row = blockIdx.x;  // b * Hq + h
   const int b = static_cast<int>(row / Hq);
   const int h = static_cast<int>(row - static_cast<long long>(b) * Hq);

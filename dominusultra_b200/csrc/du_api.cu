@@ -652,7 +652,7 @@ int prefill_block_impl(const void* q, const void* k_rot, const void* v, const vo
 // Workspace of du_decode_kvcache: chunk offsets [B + 1] (int64), {len, qpos} [B] (int2), then
 // the fragment-slot partials, o [(units + grid) * GT, D] and lse [(units + grid) * GT] fp32.
 struct KvcacheLayout {
-  size_t pre, lenq, o, lse, total;
+  size_t pre, lenq, flag, o, lse, total;
 };
 
 KvcacheLayout kvcache_layout(const DecodePlan& pl, int B, int D, int grid) {
@@ -661,7 +661,8 @@ KvcacheLayout kvcache_layout(const DecodePlan& pl, int B, int D, int grid) {
   const size_t slots = (static_cast<size_t>(pl.n_units) + grid) * pl.GT;
   ly.pre = 0;
   ly.lenq = up(sizeof(long long) * (static_cast<size_t>(B) + 1));
-  ly.o = ly.lenq + up(sizeof(int) * 2 * static_cast<size_t>(B));
+  ly.flag = ly.lenq + up(sizeof(int) * 2 * static_cast<size_t>(B));
+  ly.o = ly.flag + 256;
   ly.lse = ly.o + up(slots * D * sizeof(float));
   ly.total = ly.lse + slots * sizeof(float);
   return ly;
@@ -710,6 +711,11 @@ int decode_kvcache_impl(const void* q, const void* k_new, const void* v_new, voi
   pp.ub = Hkv * pl.n_gchunk;
   pp.append = append ? 1 : 0;
   pp.rope_positions = rope_positions;
+  pp.vl_whole = reinterpret_cast<int*>(w8 + ly.flag);
+  // Whole units are considered under the unit-count rule of plan_decode; the prep kernel then
+  // checks that the lengths spread the load evenly.
+  pp.whole_ok = (pl.GT <= 2 && 4LL * pl.n_units >= 3LL * sm_count()) ? 1 : 0;
+  pp.grid = grid;
   // One CTA scans the lengths; the append spreads over enough CTAs for a 16-byte piece each.
   const long long pieces = append ? static_cast<long long>(B) * Hkv * (D / 8) : 0;
   long long pgrid = (pieces + 255) / 256;
@@ -741,6 +747,8 @@ int decode_kvcache_impl(const void* q, const void* k_new, const void* v_new, voi
   prm.lse_part = reinterpret_cast<float*>(w8 + ly.lse);
   prm.pre = pp.pre;
   prm.lenq = pp.lenq;
+  prm.vl_whole = pp.vl_whole;
+  prm.out = out;
   prm.B = B;
   prm.ub = pp.ub;
   prm.varlen = 1;
@@ -751,7 +759,8 @@ int decode_kvcache_impl(const void* q, const void* k_new, const void* v_new, voi
   e = launch_kernel(du::decode_merge_varlen_kernel, static_cast<unsigned>(static_cast<long long>(B) * Hq),
                     128, 0, st, true, static_cast<const float*>(prm.o_part),
                     static_cast<const float*>(prm.lse_part), static_cast<const long long*>(pp.pre),
-                    Hq, Hkv, pl.GT, pp.ub, B, D, grid, out, dtype);
+                    static_cast<const int*>(pp.vl_whole), Hq, Hkv, pl.GT, pp.ub, B, D, grid, out,
+                    dtype);
   if (e != cudaSuccess) return cuda_fail(e, "decode merge launch");
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "decode merge launch");

@@ -176,3 +176,53 @@ def test_kvcache_out_of_range_lengths_are_reported(cuda_device):
                                             kn[[0, 3]], vn[[0, 3]], num_kv_heads=Hkv)
     assert max_abs(out[[0, 3]], ref) <= OUT_TOL
     assert torch.equal(kd.cpu()[[1, 2]], kc[[1, 2]]) and torch.equal(kd.cpu()[[0, 3]], kref)
+
+
+def test_kvcache_whole_units_and_split_walk_in_one_graph(cuda_device):
+    """128 one-head units: near-uniform lengths take whole units (final rows straight from the
+    split kernel, the merge returns at once), a skewed length set on the same shape takes the
+    length-balanced split walk. Both are replayed from one captured graph and checked against
+    the oracle; the mode word the prep kernel writes (after the chunk offsets and lengths in the
+    workspace) shows which path ran."""
+    from dominusultra_b200 import attention as A
+
+    B, Hq, Hkv, Lmax, D = 8, 16, 16, 1024, 64
+    dtype = torch.bfloat16
+    q, kc, vc, _, _, cos, sin = _inputs(B, Hq, Hkv, Lmax, D, dtype, 41)
+    kd, vd, cd, sd, qd = kc.cuda(), vc.cuda(), cos.cuda(), sin.cuda(), q.cuda()
+    knd = torch.empty((B, Hkv, 1, D), dtype=dtype, device="cuda")
+    vnd = torch.empty_like(knd)
+    seqlens = torch.zeros(B, dtype=torch.int32, device="cuda")
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(st):
+        dominus_ultra_decode_kvcache(qd, kd.clone(), vd.clone(), cd, sd, seqlens, knd, vnd,
+                                     num_kv_heads=Hkv)
+        st.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=st):
+            out = dominus_ultra_decode_kvcache(qd, kd, vd, cd, sd, seqlens, knd, vnd,
+                                               num_kv_heads=Hkv)
+    ws = A._WORKSPACES[("decode_kvcache", torch.cuda.current_device(), st.cuda_stream)]
+    flag_at = 2 * 256  # offsets [B+1] int64 and {len, qpos} [B], each padded to 256 bytes
+    kref, vref = kc.clone(), vc.clone()
+    cases = [([900, 905, 890, 899, 910, 880, 902, 895], 1),
+             ([1000, 3, 5, 0, 7, 2, 1, 4], 0),
+             ([700, 702, 698, 705, 699, 701, 703, 700], 1)]
+    for step, (lens, whole) in enumerate(cases):
+        kn = randn((B, Hkv, 1, D), 500 + step, dtype)
+        vn = randn((B, Hkv, 1, D), 600 + step, dtype)
+        with torch.cuda.stream(st):
+            seqlens.copy_(torch.tensor(lens, dtype=torch.int32))
+            knd.copy_(kn)
+            vnd.copy_(vn)
+            graph.replay()
+        st.synchronize()
+        mode = int(ws[flag_at:flag_at + 4].view(torch.int32).item())
+        assert mode == whole, (step, mode)
+        ref, kref, vref = oracle.decode_kvcache(q, kref, vref, cos, sin, lens, kn, vn,
+                                                num_kv_heads=Hkv)
+        assert max_abs(out, ref) <= OUT_TOL, step
+        assert torch.equal(kd.cpu(), kref) and torch.equal(vd.cpu(), vref), step
+    del graph
+    assert_no_device_timeouts()
