@@ -173,6 +173,24 @@ cudaError_t ensure_smem_attr(Kern kern, int bytes) {
   return e;
 }
 
+// Launch on `st`; with `pdl` as a programmatic dependent of the stream's previous kernel (the
+// kernel must call griddep_wait before touching that kernel's outputs).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kern)(KArgs...), dim3 grid, unsigned block, size_t smem,
+                          cudaStream_t st, bool pdl, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 // Launch the standalone rotary kernel over rows = B * H * T rows of D elements.
 template <bool BF16, bool OUT_F16, bool BACKWARD>
 int launch_rope_t(const du::RopeParams& rp, cudaStream_t st) {
@@ -242,7 +260,11 @@ int launch_fa_t(const void* q, const void* k_rot, const void* v, du::PrefillPara
   cudaError_t e = ensure_smem_attr(kern, S::SMEM_BYTES);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(prefill)");
   dim3 grid(static_cast<unsigned>(B * prm.Hq), static_cast<unsigned>(prm.n_qtiles));
-  kern<<<grid, S::NTHREADS, S::SMEM_BYTES, st>>>(tq, tk, tv, prm);
+  // The whole-sequence path follows its key-rotation launch as a programmatic dependent: the
+  // CTAs' set-up and query loads overlap the rotation; only the K producer waits for it. The
+  // block form (context-parallel prefill) is launched after arbitrary work and does not.
+  e = launch_kernel(kern, grid, S::NTHREADS, S::SMEM_BYTES, st, !BLOCK, tq, tk, tv, prm);
+  if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
   return DU_OK;
@@ -292,7 +314,8 @@ int launch_prefill_t(const void* q, const void* k, const void* v, du::PrefillPar
       e = ensure_smem_attr(kern1, S1::SMEM_BYTES);
       if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(prefill)");
       dim3 grid1(static_cast<unsigned>(B * prm.Hq), static_cast<unsigned>(prm.n_qtiles));
-      kern1<<<grid1, S1::NTHREADS, S1::SMEM_BYTES, st>>>(tq, tk, tv, prm);
+      e = launch_kernel(kern1, grid1, S1::NTHREADS, S1::SMEM_BYTES, st, true, tq, tk, tv, prm);
+      if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
       e = cudaGetLastError();
       if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
       return DU_OK;
@@ -403,24 +426,6 @@ size_t decode_ws_bytes(const DecodePlan& pl, int B, int Hq, int D) {
   const size_t o = rows * pl.n_split * D * sizeof(float);
   const size_t l = rows * pl.n_split * sizeof(float);
   return ((o + 255) / 256) * 256 + l;
-}
-
-// Launch on `st`; with `pdl` as a programmatic dependent of the stream's previous kernel (the
-// kernel must call griddep_wait before touching that kernel's outputs).
-template <typename... KArgs, typename... Args>
-cudaError_t launch_kernel(void (*kern)(KArgs...), unsigned grid, unsigned block, size_t smem,
-                          cudaStream_t st, bool pdl, Args&&... args) {
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(block);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 template <int D, bool BF16, int GT>

@@ -286,6 +286,9 @@ __global__ void __launch_bounds__(256, 2)
     regs_dec<S::REG_OTHER>();
     if (lane == 0) {
       int issued = 0;
+      // The rotated keys come from the preceding rotary launch (this kernel may start before
+      // it completes); nothing else this CTA reads is written by it.
+      griddep_wait();
       for (int j = 0; j < nk; ++j) {
         const int s = j % NSK;
         if (j >= NSK && !mbar_wait(BAR_KE(s), (j / NSK - 1) & 1, failed, 410)) break;

@@ -403,6 +403,9 @@ __global__ void __launch_bounds__(384, 1)
     regs_dec<S::REG_OTHER>();
     if (lane == 0) {
       int issued = 0;  // (the query tiles were issued before the CTA barrier)
+      // The rotated keys come from the preceding rotary launch (this kernel may start before
+      // it completes); nothing else this CTA reads is written by it.
+      griddep_wait();
       for (int j = 0; j < nk_all; ++j) {
         const int s = j % NSK;
         if (j >= NSK && !mbar_wait(BAR_KE(s), (j / NSK - 1) & 1, failed, 310)) break;

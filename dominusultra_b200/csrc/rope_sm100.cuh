@@ -35,6 +35,7 @@ struct RopeParams {
 
 template <bool BF16, bool OUT_F16, bool BACKWARD>
 __global__ void __launch_bounds__(256) rope_kernel(const RopeParams p) {
+  griddep_launch_dependents();  // a prefill's attention launch may start its set-up now
   const int cpr = p.D / 16;  // chunk pairs per row
   const long long total = p.rows * cpr;
   const uint8_t* xb = static_cast<const uint8_t*>(p.x);
