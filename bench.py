@@ -567,10 +567,13 @@ def main():
     flops = prefill_flops(B, H, S, D)
     value = world * flops / (ms_step / 1000.0) / 1e12
 
-    # The dominant kernel alone: a step is the key-rotation launch plus the attention launch;
-    # the rotation is timed on its own (same sizes, same workspace) and taken off.
+    # The dominant kernel: a step is the key-rotation launch plus the attention launch, and the
+    # attention launch starts (as a programmatic dependent) while the rotation runs, so events
+    # cannot separate them. The step time bounds the attention launch's duration from above:
+    # achieved = algorithmic FLOPs / step time is a lower bound on the kernel's rate. The
+    # rotation pass is timed on its own for reference.
     rope_ms = rope_pass_ms(sets, cos, sin, cfg, args.steps, side)
-    attn_ms = max(ms_step - rope_ms, 1e-6)
+    attn_ms = ms_step
     achieved = flops / (attn_ms / 1000.0) / 1e12
 
     # End to end through the public API with pinned host buffers.
@@ -681,6 +684,8 @@ def main():
                 "frac": achieved / peak, "traffic": NCU_TRAFFIC["prefill"],
                 "peak_kind": f"{peak_kind} bf16 dense (burst)",
                 "kernel": "prefill_fa1_kernel", "kernel_ms": attn_ms,
+                "kernel_ms_is": "the step time (rotation overlapped with the attention launch): "
+                                "an upper bound on the attention launch",
                 "algorithmic_flops": flops,
                 "rope_pass": {"kernel": "rope_kernel (keys, bf16 -> fp16)", "ms": rope_ms,
                               "gbs": rope_bytes(cfg) / (rope_ms / 1000.0) / 1e9},
