@@ -17,6 +17,7 @@
 
 #include "../../include/dominus_ultra_b200.h"
 #include "decode_sm100.cuh"
+#include "decode_tc_sm100.cuh"
 #include "prefill_fa1_sm100.cuh"
 #include "prefill_fa_sm100.cuh"
 #include "prefill_sm100.cuh"
@@ -366,7 +367,12 @@ int decode_chunk_d(int GT) {
   }
 }
 
-int decode_chunk(int D, int GT) {
+// Four-head units at head_dim 128 run on the tensor-core kernel (decode_tc_sm100.cuh), except
+// for the per-sequence-length walk of du_decode_kvcache.
+bool decode_use_tc(int D, int GT) { return D == 128 && GT == 4; }
+
+int decode_chunk(int D, int GT, bool tc = false) {
+  if (tc && decode_use_tc(D, GT)) return du::DecodeTcShape::CK;
   switch (D) {
     case 16: return decode_chunk_d<16>(GT);
     case 32: return decode_chunk_d<32>(GT);
@@ -392,7 +398,7 @@ DecodePlan plan_decode(int B, int Hq, int Hkv, int L, int D) {
   pl.n_gchunk = G / pl.GT;
   const long long units = static_cast<long long>(B) * Hkv * pl.n_gchunk;
   const long long ctas = static_cast<long long>(sm_count()) * decode_residency(pl.GT);
-  const int chunk = decode_chunk(D, pl.GT);
+  const int chunk = decode_chunk(D, pl.GT, true);
   pl.n_units = static_cast<int>(units);
   pl.cpu = (L + chunk - 1) / chunk;
   pl.total_chunks = units * pl.cpu;
@@ -428,9 +434,37 @@ size_t decode_ws_bytes(const DecodePlan& pl, int B, int Hq, int D) {
   return ((o + 255) / 256) * 256 + l;
 }
 
+template <bool BF16>
+int launch_decode_tc_t(const du::DecodeParams& prm, int B, long long rope_positions, int grid,
+                       cudaStream_t st) {
+  using S = du::DecodeTcShape;
+  const int dtype = BF16 ? DU_DTYPE_BF16 : DU_DTYPE_F16;
+  CUtensorMap tk, tv, tc, ts;
+  int rc;
+  const long long units = static_cast<long long>(B) * prm.Hkv;
+  if ((rc = encode_map(&tk, prm.k, dtype, S::D, prm.L, units, S::SPAN / 2, S::CK, S::SPAN)) != DU_OK) return rc;
+  if ((rc = encode_map(&tv, prm.v, dtype, S::D, prm.L, units, S::SPAN / 2, S::CK, S::SPAN)) != DU_OK) return rc;
+  if ((rc = encode_map_2d_sw(&tc, prm.cos, dtype, S::D / 2, rope_positions, S::D / 2, S::CK, S::SPAN)) != DU_OK)
+    return rc;
+  if ((rc = encode_map_2d_sw(&ts, prm.sin, dtype, S::D / 2, rope_positions, S::D / 2, S::CK, S::SPAN)) != DU_OK)
+    return rc;
+  auto kern = du::decode_tc_kernel<S::D, BF16, S::GT>;
+  cudaError_t e = ensure_smem_attr(kern, S::SMEM_BYTES);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(decode, tensor cores)");
+  e = launch_kernel(kern, dim3(static_cast<unsigned>(grid)), S::NTHREADS, S::SMEM_BYTES, st, false,
+                    tk, tv, tc, ts, prm);
+  if (e != cudaSuccess) return cuda_fail(e, "decode launch");
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "decode launch");
+  return DU_OK;
+}
+
 template <int D, bool BF16, int GT>
 int launch_decode_split_t(const du::DecodeParams& prm, int B, long long rope_positions, int grid,
                           cudaStream_t st) {
+  if constexpr (D == 128 && GT == 4) {
+    if (!prm.varlen) return launch_decode_tc_t<BF16>(prm, B, rope_positions, grid, st);
+  }
   using S = du::DecodeShape<D, GT>;
   const int dtype = BF16 ? DU_DTYPE_BF16 : DU_DTYPE_F16;
   CUtensorMap tk, tv, tc, ts;
