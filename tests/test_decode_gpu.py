@@ -158,3 +158,41 @@ def test_decode_single_token_and_shape(cuda_device):
     assert out.shape == (1, 8, 1, 64) and torch.isfinite(out.float()).all()
     # with one cached key the output is exactly that key's value row
     assert max_abs(out[:, :, 0], v[:, :, 0]) == 0.0
+
+
+TC_CASES = [
+    # B, Hq, Hkv, L, dtype: four query heads per KV head at head_dim 128 (the tcgen05 kernel)
+    (2, 8, 2, 1, torch.bfloat16),        # one key: a chunk of 128 rows with 127 masked
+    (2, 8, 2, 127, torch.float16),
+    (1, 16, 4, 128, torch.bfloat16),     # exactly one chunk
+    (1, 16, 4, 129, torch.bfloat16),     # one key into the second chunk
+    (40, 32, 8, 300, torch.bfloat16),    # 320 units: several whole units per CTA
+    (2, 32, 8, 20000, torch.bfloat16),   # long split walk, fragments across units
+    (1, 64, 16, 2500, torch.float16),
+]
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,L,dtype", TC_CASES)
+def test_decode_four_head_units_tensor_core(cuda_device, B, Hq, Hkv, L, dtype):
+    D = 128
+    q, k, v, cos, sin = _inputs(B, Hq, Hkv, L, D, dtype, seed=L + B, base=500000.0)
+    out = dominus_ultra_decode(q.cuda(), k.cuda(), v.cuda(), cos.cuda(), sin.cuda(), num_kv_heads=Hkv)
+    torch.cuda.synchronize()
+    ref = oracle.decode(q, k, v, cos, sin, Hkv)
+    assert_no_device_timeouts()
+    assert max_abs(out, ref) <= OUT_TOL
+
+
+def test_decode_four_head_partial_outputs(cuda_device):
+    """du_decode_partial on a shard at a position offset (fp32 out and LSE, the multi-GPU path)
+    through the tensor-core kernel, whole-unit and split plans."""
+    for B, L in ((40, 256), (2, 9000)):
+        Hq, Hkv, D, off = 32, 8, 128, 777
+        q, k, v, _, _ = _inputs(B, Hq, Hkv, L, D, torch.bfloat16, seed=5 + B)
+        cos, sin = precompute_rope_cos_sin(off + L + 1, D, "cpu", torch.bfloat16, 500000.0)
+        o, lse = decode_partial(q.cuda(), k.cuda(), v.cuda(), cos.cuda(), sin.cuda(), Hkv,
+                                off + L, off)
+        torch.cuda.synchronize()
+        ro, rl = oracle.decode_partial(q, k, v, cos, sin, Hkv, q_pos=off + L, kv_pos_offset=off)
+        assert_no_device_timeouts()
+        assert max_abs(o, ro) <= OUT_TOL and max_abs(lse, rl) <= LSE_TOL
