@@ -172,6 +172,13 @@ __global__ void __launch_bounds__(224, 1)
   __syncthreads();
   tc_fence_after();
 
+  // Per-sequence lengths: the prep kernel (this launch's programmatic predecessor) has written
+  // the chunk offsets and the appended cache rows once this returns.
+  if (p.varlen) {
+    griddep_wait();
+    fence_proxy_async_global();  // the appended rows are read by TMA (async proxy)
+  }
+
   const uint8_t* cosb = static_cast<const uint8_t*>(p.cos);
   const uint8_t* sinb = static_cast<const uint8_t*>(p.sin);
 
@@ -270,9 +277,11 @@ __global__ void __launch_bounds__(224, 1)
       umma_commit(BAR_SF);
       umma_commit(EMPTY(gg % S::NSTG));  // the rotated keys and the tables are read
     };
-    for (; ok && walk.next(p, CK, fr); ++it) {
+    for (; ok && walk.next(p, CK, fr);) {
       const int n = (fr.kend - fr.kbeg + CK - 1) / CK;
+      if (n == 0) continue;  // a sequence with no keys: nothing to multiply
       ok = __all_sync(0xffffffffu, mbar_wait(BAR_QR, it & 1, failed, 710));
+      ++it;  // non-empty fragments (QR phases)
       if (ok) ok = __all_sync(0xffffffffu, mbar_wait(RK(g & 1), (g >> 1) & 1, failed, 711));
       if (ok && g > 0) ok = __all_sync(0xffffffffu, mbar_wait(BAR_SC, (g - 1) & 1, failed, 712));
       if (!ok) break;
@@ -355,12 +364,47 @@ __global__ void __launch_bounds__(224, 1)
     DecodeWalk walk;
     walk.init(p);
     DecodeFrag fr;
+    int qf = 0;  // non-empty fragments (QR and MRG phases)
+    // The unit's output row gg, dimension d = tid, value val, natural-log lse (thread 0).
+    auto emit = [&](const DecodeFrag& f, size_t orow, int gg, float val, float lse) {
+      if (p.varlen && f.slot >= 0) {
+        const size_t fs = static_cast<size_t>(f.slot) * GT + gg;  // fragment slot row
+        p.o_part[fs * D + tid] = val;
+        if (tid == 0) p.lse_part[fs] = lse;
+      } else if (p.mode == 0 || f.slot < 0) {
+        if constexpr (BF16) {
+          static_cast<__nv_bfloat16*>(p.out)[orow * D + tid] = __float2bfloat16_rn(val);
+        } else {
+          static_cast<__half*>(p.out)[orow * D + tid] = __float2half_rn(val);
+        }
+      } else {
+        p.o_part[(orow * p.n_split + f.slot) * D + tid] = val;
+        if (tid == 0) p.lse_part[orow * p.n_split + f.slot] = lse;
+        if (f.last)  // the row's unused slots weigh nothing in the merge
+          for (int sl = f.slot + 1; sl < p.n_split; ++sl) {
+            p.o_part[(orow * p.n_split + sl) * D + tid] = 0.f;
+            if (tid == 0) p.lse_part[orow * p.n_split + sl] = -INFINITY;
+          }
+      }
+    };
     for (; ok && walk.next(p, CK, fr); ++it) {
       const int gch = fr.unit % p.n_gchunk;
       const int bk = fr.unit / p.n_gchunk;
       const int b = bk / p.Hkv;
       const int h0 = (bk - b * p.Hkv) * p.G + gch * GT;
       const int n = (fr.kend - fr.kbeg + CK - 1) / CK;
+      if (n == 0) {
+        // A sequence with no keys (per-sequence lengths): release its header, zero output.
+        if (warp == 0) {
+          const int hs = it % S::NHDR;
+          ok = __all_sync(0xffffffffu, mbar_wait(HFULL(hs), (it / S::NHDR) & 1, failed, 728));
+          if (ok) mbar_arrive(HEMPTY(hs));
+        }
+#pragma unroll
+        for (int h = 0; h < GT; ++h)
+          emit(fr, static_cast<size_t>(b) * p.Hq + h0 + h, h, 0.f, -INFINITY);
+        continue;
+      }
       if (warp == 0) {
         // The unit's queries, rotated at the query position into the fp16 query tile.
         const int hs = it % S::NHDR;
@@ -488,7 +532,8 @@ __global__ void __launch_bounds__(224, 1)
       }
       tc_fence_before();
       mbar_arrive(BAR_MRG);
-      ok = __all_sync(0xffffffffu, mbar_wait(BAR_MRG, it & 1, failed, 727));
+      ok = __all_sync(0xffffffffu, mbar_wait(BAR_MRG, qf & 1, failed, 727));
+      ++qf;
       if (!ok) break;
       // Thread d writes dimension d of the unit's GT rows.
       const float* mw = mrg + 4 * GT * D;
@@ -506,23 +551,8 @@ __global__ void __launch_bounds__(224, 1)
           A += mrg[(w2 * GT + h) * D + tid] * wt;
         }
         const size_t orow = static_cast<size_t>(b) * p.Hq + h0 + h;
-        const float val = (L > 0.f) ? A / L : 0.f;
-        if (p.mode == 0) {
-          if constexpr (BF16) {
-            static_cast<__nv_bfloat16*>(p.out)[orow * D + tid] = __float2bfloat16_rn(val);
-          } else {
-            static_cast<__half*>(p.out)[orow * D + tid] = __float2half_rn(val);
-          }
-        } else {
-          p.o_part[(orow * p.n_split + fr.slot) * D + tid] = val;
-          if (tid == 0)
-            p.lse_part[orow * p.n_split + fr.slot] = (L > 0.f) ? (M + lg2(L)) * 0.69314718055994531f : -INFINITY;
-          if (fr.last)  // the row's unused slots weigh nothing in the merge
-            for (int sl = fr.slot + 1; sl < p.n_split; ++sl) {
-              p.o_part[(orow * p.n_split + sl) * D + tid] = 0.f;
-              if (tid == 0) p.lse_part[orow * p.n_split + sl] = -INFINITY;
-            }
-        }
+        emit(fr, orow, h, (L > 0.f) ? A / L : 0.f,
+             (L > 0.f) ? (M + lg2(L)) * 0.69314718055994531f : -INFINITY);
       }
     }
   }

@@ -367,8 +367,8 @@ int decode_chunk_d(int GT) {
   }
 }
 
-// Four-head units at head_dim 128 run on the tensor-core kernel (decode_tc_sm100.cuh), except
-// for the per-sequence-length walk of du_decode_kvcache.
+// Four-head units at head_dim 128 run on the tensor-core kernel (decode_tc_sm100.cuh), for
+// du_decode, du_decode_partial and du_decode_kvcache alike.
 bool decode_use_tc(int D, int GT) { return D == 128 && GT == 4; }
 
 int decode_chunk(int D, int GT, bool tc = false) {
@@ -451,7 +451,9 @@ int launch_decode_tc_t(const du::DecodeParams& prm, int B, long long rope_positi
   auto kern = du::decode_tc_kernel<S::D, BF16, S::GT>;
   cudaError_t e = ensure_smem_attr(kern, S::SMEM_BYTES);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(decode, tensor cores)");
-  e = launch_kernel(kern, dim3(static_cast<unsigned>(grid)), S::NTHREADS, S::SMEM_BYTES, st, false,
+  // With per-sequence lengths the kernel follows decode_prep_kernel as its programmatic dependent.
+  e = launch_kernel(kern, dim3(static_cast<unsigned>(grid)), S::NTHREADS, S::SMEM_BYTES, st,
+                    prm.varlen != 0,
                     tk, tv, tc, ts, prm);
   if (e != cudaSuccess) return cuda_fail(e, "decode launch");
   e = cudaGetLastError();
@@ -462,9 +464,7 @@ int launch_decode_tc_t(const du::DecodeParams& prm, int B, long long rope_positi
 template <int D, bool BF16, int GT>
 int launch_decode_split_t(const du::DecodeParams& prm, int B, long long rope_positions, int grid,
                           cudaStream_t st) {
-  if constexpr (D == 128 && GT == 4) {
-    if (!prm.varlen) return launch_decode_tc_t<BF16>(prm, B, rope_positions, grid, st);
-  }
+  if constexpr (D == 128 && GT == 4) return launch_decode_tc_t<BF16>(prm, B, rope_positions, grid, st);
   using S = du::DecodeShape<D, GT>;
   const int dtype = BF16 ? DU_DTYPE_BF16 : DU_DTYPE_F16;
   CUtensorMap tk, tv, tc, ts;
@@ -746,7 +746,7 @@ int decode_kvcache_impl(const void* q, const void* k_new, const void* v_new, voi
   pp.Hkv = Hkv;
   pp.L = L;
   pp.D = D;
-  pp.CK = decode_chunk(D, pl.GT);
+  pp.CK = decode_chunk(D, pl.GT, true);  // the chunk of the kernel the walk runs on
   pp.ub = Hkv * pl.n_gchunk;
   pp.append = append ? 1 : 0;
   pp.rope_positions = rope_positions;
