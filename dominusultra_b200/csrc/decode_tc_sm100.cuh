@@ -27,37 +27,45 @@
 
 namespace du {
 
+template <int D_>
 struct DecodeTcShape {
-  static constexpr int D = 128;
+  static constexpr int D = D_;
   static constexpr int GT = 4;
   static constexpr int NQ = 16;     // rows of the query tile (N of S^T)
   static constexpr int CK = 128;    // keys per chunk (M of S^T)
-  static constexpr int SPAN = 128;
+  static constexpr int SPAN = 128;  // K / V / query rows: 64-element blocks of 128 bytes
+  static constexpr int NBLK = 2 * D / SPAN;
+  static constexpr int TSPAN = D;   // cos / sin rows: D/2 16-bit values
+  static constexpr int PAIRS = D / 16;  // 16-byte chunk pairs (i, i + D/2) per row
   static constexpr int ROWB = 2 * D;
-  static constexpr int KV_BYTES = CK * ROWB;     // 32 KB: two 64-element column blocks
-  static constexpr int TAB_BYTES = CK * D;       // 16 KB: CK rows of D/2 16-bit values
+  static constexpr int KV_BYTES = CK * ROWB;
+  static constexpr int TAB_BYTES = CK * TSPAN;
   // Two rings: K with the cos / sin rows of its keys (freed once QK has read the rotated keys)
-  // and V (freed after PV), each two stages deep, refilled by their own TMA warps.
+  // and V (freed after PV), refilled by their own TMA warps.
   static constexpr int OFF_K = 0;                  // within a K stage
   static constexpr int OFF_C = KV_BYTES;
   static constexpr int OFF_S = OFF_C + TAB_BYTES;
-  static constexpr int KSTAGE = OFF_S + TAB_BYTES;  // 64 KB
-  static constexpr int NSTG = 2;
+  static constexpr int KSTAGE = OFF_S + TAB_BYTES;
+  static constexpr int NSTG = (D >= 128) ? 2 : 3;
   static constexpr int OFF_VR = NSTG * KSTAGE;      // V ring: NSTG x KV_BYTES
   static constexpr int OFF_Q = OFF_VR + NSTG * KV_BYTES;   // [NQ rows x D] fp16, K-major SW128
-  static constexpr int Q_BYTES = NQ * ROWB;                // 4 KB
+  static constexpr int Q_BYTES = NQ * ROWB;
   static constexpr int OFF_P = OFF_Q + Q_BYTES;            // P staging [4 warps][GT][32] 16-bit
   static constexpr int P_BYTES = 4 * GT * 32 * 2;
   static constexpr int NHDR = 2;
   static constexpr int HDR_Q = GT * ROWB;
-  static constexpr int HDR = HDR_Q + 2 * (D / 2) * 2;      // q rows + cos row + sin row
+  static constexpr int HDR = HDR_Q + 2 * TSPAN;           // q rows + cos row + sin row
   static constexpr int OFF_HDR = OFF_P + P_BYTES;
   static constexpr int OFF_MRG = OFF_HDR + NHDR * HDR;     // [4 warps][GT][D] o, then m, l
   static constexpr int MRG_BYTES = 4 * GT * D * 4 + 2 * 4 * GT * 4;
   static constexpr int OFF_BAR = OFF_MRG + MRG_BYTES;
-  // kfull[2], kempty[2], rk[2] (at 16, 17), sf, sc, od[2], qr, mrg, hfull[2], hempty[2], drain,
-  // pf[2] (at 18, 19), vfull[2], vempty[2]
-  static constexpr int N_BAR = 24;
+  // full, empty, vfull, vempty, rk: one per stage; then sf, sc, od[2], pf[2], qr, mrg,
+  // hfull[2], hempty[2], drain
+  static constexpr int B_FULL = 0, B_EMPTY = NSTG, B_VFULL = 2 * NSTG, B_VEMPTY = 3 * NSTG,
+                       B_RK = 4 * NSTG, B_SF = 5 * NSTG, B_SC = B_SF + 1, B_OD = B_SF + 2,
+                       B_PF = B_SF + 4, B_QR = B_SF + 6, B_MRG = B_SF + 7, B_HFULL = B_SF + 8,
+                       B_HEMPTY = B_SF + 10, B_DR = B_SF + 12;
+  static constexpr int N_BAR = B_DR + 1;
   static constexpr int OFF_MISC = OFF_BAR + 8 * N_BAR;     // tmem address, failure flag
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
   static constexpr int TMEM_COLS = 512;
@@ -65,7 +73,9 @@ struct DecodeTcShape {
   static constexpr int TM_P = 64;   // P[2]: CK / 2 packed columns each
   static constexpr int TM_O = 256;  // O: D fp32 columns (lanes 32w + h: warp w's partial of head h)
   static constexpr int NTHREADS = 224;
-  static_assert(KSTAGE % 1024 == 0 && OFF_Q % 1024 == 0 && Q_BYTES % 1024 == 0, "swizzled tile alignment");
+  static_assert(D == 64 || D == 128, "tensor-core decode: head_dim 64 or 128");
+  static_assert(KSTAGE % 1024 == 0 && KV_BYTES % 1024 == 0 && OFF_Q % 1024 == 0 &&
+                    Q_BYTES % 1024 == 0, "swizzled tile alignment");
   static_assert(OFF_HDR % 128 == 0 && HDR % 128 == 0 && OFF_MRG % 16 == 0, "header alignment");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
   static_assert(TM_P + CK <= TM_O && TM_O + D <= TMEM_COLS, "TMEM budget");
@@ -85,9 +95,9 @@ __global__ void __launch_bounds__(224, 1)
     decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                      const __grid_constant__ CUtensorMap tm_cos, const __grid_constant__ CUtensorMap tm_sin,
                      const DecodeParams p) {
-  using S = DecodeTcShape;
-  static_assert(D == S::D && GT == S::GT, "tensor-core decode: head_dim 128, four heads per unit");
-  constexpr int CK = S::CK, SPAN = S::SPAN, NQ = S::NQ, HALF = D / 2;
+  using S = DecodeTcShape<D>;
+  static_assert(GT == S::GT, "tensor-core decode: four heads per unit");
+  constexpr int CK = S::CK, SPAN = S::SPAN, NQ = S::NQ, PAIRS = S::PAIRS;
   constexpr uint32_t SWZ = swizzle_code(SPAN);
   constexpr uint32_t IDESC_QK = idesc_f16(128, NQ, 0, 0, 0, 0);  // fp16 R(K) x fp16 R(Q)
   constexpr uint32_t IDESC_PV = idesc_f16(128, D, BF16 ? 1 : 0, BF16 ? 1 : 0, 0, 1);
@@ -97,23 +107,23 @@ __global__ void __launch_bounds__(224, 1)
   const uint32_t sbase = (raw_u32 + 1023u) & ~1023u;
   uint8_t* sgen = smem_raw + (sbase - raw_u32);
   auto bar = [&](int i) -> uint32_t { return sbase + S::OFF_BAR + 8u * static_cast<uint32_t>(i); };
-  auto FULL = [&](int s) { return bar(s); };        // K + tables of a stage landed
-  auto EMPTY = [&](int s) { return bar(2 + s); };       // QK read it
-  auto VFULL = [&](int s) { return bar(20 + s); };
-  auto VEMPTY = [&](int s) { return bar(22 + s); };     // PV read it
-  const uint32_t BAR_SF = bar(5), BAR_SC = bar(6);
-  // K of even / odd chunks rotated. One barrier per stage: at a fragment boundary the MMA warp
-  // checks the next fragment's first chunk only after its last PV, by which time the next two
-  // chunks may both be rotated; per-stage barriers cannot complete twice before that check.
-  auto RK = [&](int i) { return bar(16 + i); };
+  auto FULL = [&](int s) { return bar(S::B_FULL + s); };      // K + tables of a stage landed
+  auto EMPTY = [&](int s) { return bar(S::B_EMPTY + s); };    // QK read it
+  auto VFULL = [&](int s) { return bar(S::B_VFULL + s); };
+  auto VEMPTY = [&](int s) { return bar(S::B_VEMPTY + s); };  // PV read it
+  // K of a stage rotated. One barrier per stage: at a fragment boundary the MMA warp checks the
+  // next fragment's first chunk only after its last PV, by which time later chunks may be
+  // rotated too; rotating the stage's next chunk needs this chunk's QK, issued after the check.
+  auto RK = [&](int s) { return bar(S::B_RK + s); };
+  const uint32_t BAR_SF = bar(S::B_SF), BAR_SC = bar(S::B_SC);
   // P of even / odd chunks written (one barrier per P buffer: the MMA warp issues the next QK
   // before waiting for this chunk's P, so a single barrier could complete twice unseen).
-  auto PF = [&](int i) { return bar(18 + i); };
-  auto OD = [&](int i) { return bar(7 + i); };  // PV of even / odd chunks complete
-  const uint32_t BAR_QR = bar(9), BAR_MRG = bar(10);
-  auto HFULL = [&](int i) { return bar(11 + i); };
-  auto HEMPTY = [&](int i) { return bar(13 + i); };
-  const uint32_t BAR_DR = bar(15);
+  auto PF = [&](int i) { return bar(S::B_PF + i); };
+  auto OD = [&](int i) { return bar(S::B_OD + i); };  // PV of even / odd chunks complete
+  const uint32_t BAR_QR = bar(S::B_QR), BAR_MRG = bar(S::B_MRG);
+  auto HFULL = [&](int i) { return bar(S::B_HFULL + i); };
+  auto HEMPTY = [&](int i) { return bar(S::B_HEMPTY + i); };
+  const uint32_t BAR_DR = bar(S::B_DR);
   const uint32_t tmem_slot = sbase + S::OFF_MISC;
   volatile int* failed = reinterpret_cast<volatile int*>(sgen + S::OFF_MISC + 4);
   float* mrg = reinterpret_cast<float*>(sgen + S::OFF_MRG);  // o [4][GT][D], m [4][GT], l [4][GT]
@@ -134,8 +144,7 @@ __global__ void __launch_bounds__(224, 1)
       mbar_init(VFULL(s), 1);
       mbar_init(VEMPTY(s), 1);
     }
-    mbar_init(RK(0), 128);
-    mbar_init(RK(1), 128);
+    for (int s = 0; s < S::NSTG; ++s) mbar_init(RK(s), 128);
     mbar_init(BAR_SF, 1);
     mbar_init(BAR_SC, 128);
     mbar_init(PF(0), 128);
@@ -201,12 +210,12 @@ __global__ void __launch_bounds__(224, 1)
         const int b = bk / p.Hkv;
         const int h0 = (bk - b * p.Hkv) * p.G + gch * GT;
         const uint32_t hd = sbase + S::OFF_HDR + hs * S::HDR;
-        const size_t trow = static_cast<size_t>(fr.qpos) * D;  // D/2 16-bit values per row
+        const size_t trow = static_cast<size_t>(fr.qpos) * S::TSPAN;  // D/2 16-bit values per row
         mbar_expect_tx(HFULL(hs), static_cast<uint32_t>(S::HDR));
         bulk_load(hd, static_cast<const uint8_t*>(p.q) + (static_cast<size_t>(b) * p.Hq + h0) * S::ROWB,
                   S::HDR_Q, HFULL(hs));
-        bulk_load(hd + S::HDR_Q, cosb + trow, D, HFULL(hs));
-        bulk_load(hd + S::HDR_Q + D, sinb + trow, D, HFULL(hs));
+        bulk_load(hd + S::HDR_Q, cosb + trow, S::TSPAN, HFULL(hs));
+        bulk_load(hd + S::HDR_Q + S::TSPAN, sinb + trow, S::TSPAN, HFULL(hs));
         for (int c0 = fr.kbeg; c0 < fr.kend; c0 += CK, ++g) {
           const int s = g % S::NSTG;
           if (g >= S::NSTG && !mbar_wait(EMPTY(s), ((g / S::NSTG) - 1) & 1, failed, 701)) {
@@ -217,8 +226,8 @@ __global__ void __launch_bounds__(224, 1)
           const int tpos = static_cast<int>(p.kv_pos_offset + c0);
           mbar_expect_tx(FULL(s), static_cast<uint32_t>(S::KSTAGE));
 #pragma unroll
-          for (int blk = 0; blk < 2; ++blk)
-            tma_load_3d(st + S::OFF_K + blk * CK * SPAN, &tm_k, FULL(s), blk * HALF, c0, bk);
+          for (int blk = 0; blk < S::NBLK; ++blk)
+            tma_load_3d(st + S::OFF_K + blk * CK * SPAN, &tm_k, FULL(s), blk * (SPAN / 2), c0, bk);
           tma_load_2d(st + S::OFF_C, &tm_cos, FULL(s), 0, tpos);
           tma_load_2d(st + S::OFF_S, &tm_sin, FULL(s), 0, tpos);
         }
@@ -249,8 +258,8 @@ __global__ void __launch_bounds__(224, 1)
           const uint32_t st = sbase + S::OFF_VR + s * S::KV_BYTES;
           mbar_expect_tx(VFULL(s), static_cast<uint32_t>(S::KV_BYTES));
 #pragma unroll
-          for (int blk = 0; blk < 2; ++blk)
-            tma_load_3d(st + blk * CK * SPAN, &tm_v, VFULL(s), blk * HALF, c0, bk);
+          for (int blk = 0; blk < S::NBLK; ++blk)
+            tma_load_3d(st + blk * CK * SPAN, &tm_v, VFULL(s), blk * (SPAN / 2), c0, bk);
         }
       }
       for (int j = (g > S::NSTG ? g - S::NSTG : 0); j < g; ++j)
@@ -282,7 +291,7 @@ __global__ void __launch_bounds__(224, 1)
       if (n == 0) continue;  // a sequence with no keys: nothing to multiply
       ok = __all_sync(0xffffffffu, mbar_wait(BAR_QR, it & 1, failed, 710));
       ++it;  // non-empty fragments (QR phases)
-      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(RK(g & 1), (g >> 1) & 1, failed, 711));
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(RK(g % S::NSTG), (g / S::NSTG) & 1, failed, 711));
       if (ok && g > 0) ok = __all_sync(0xffffffffu, mbar_wait(BAR_SC, (g - 1) & 1, failed, 712));
       if (!ok) break;
       tc_fence_after();
@@ -291,7 +300,7 @@ __global__ void __launch_bounds__(224, 1)
       for (int j = 0; j < n; ++j) {
         const int gj = g + j;
         if (j + 1 < n) {  // QK of the next chunk, once it is rotated and S has been read
-          ok = __all_sync(0xffffffffu, mbar_wait(RK((gj + 1) & 1), ((gj + 1) >> 1) & 1, failed, 713));
+          ok = __all_sync(0xffffffffu, mbar_wait(RK((gj + 1) % S::NSTG), ((gj + 1) / S::NSTG) & 1, failed, 713));
           if (ok) ok = __all_sync(0xffffffffu, mbar_wait(BAR_SC, gj & 1, failed, 714));
           if (!ok) break;
           tc_fence_after();
@@ -334,14 +343,15 @@ __global__ void __launch_bounds__(224, 1)
       if (!__all_sync(0xffffffffu, mbar_wait(FULL(s), (gg / S::NSTG) & 1, failed, 720))) return false;
       const uint32_t st = sbase + s * S::KSTAGE;
 #pragma unroll 2
-      for (int u = tid; u < CK * 8; u += 128) {
-        const int r = u >> 3, c = u & 7;
+      for (int u = tid; u < CK * PAIRS; u += 128) {
+        const int r = u / PAIRS, c = u % PAIRS;
         const uint32_t o1 = swz_chunk_offset<SPAN>(CK, r, c);
-        const uint32_t o2 = swz_chunk_offset<SPAN>(CK, r, c + 8);
+        const uint32_t o2 = swz_chunk_offset<SPAN>(CK, r, c + PAIRS);
+        const uint32_t ot = swz_chunk_offset<S::TSPAN>(CK, r, c);
         const uint4 k1 = ld_shared_v4(st + S::OFF_K + o1);
         const uint4 k2 = ld_shared_v4(st + S::OFF_K + o2);
-        const uint4 cv = ld_shared_v4(st + S::OFF_C + o1);
-        const uint4 sv = ld_shared_v4(st + S::OFF_S + o1);
+        const uint4 cv = ld_shared_v4(st + S::OFF_C + ot);
+        const uint4 sv = ld_shared_v4(st + S::OFF_S + ot);
         const uint32_t a[4] = {k1.x, k1.y, k1.z, k1.w}, bb[4] = {k2.x, k2.y, k2.z, k2.w};
         const uint32_t ca[4] = {cv.x, cv.y, cv.z, cv.w}, sa[4] = {sv.x, sv.y, sv.z, sv.w};
         uint32_t y1[4], y2[4];
@@ -356,7 +366,7 @@ __global__ void __launch_bounds__(224, 1)
         st_shared_v4(st + S::OFF_K + o2, make_uint4(y2[0], y2[1], y2[2], y2[3]));
       }
       fence_proxy_async_smem();
-      mbar_arrive(RK(gg & 1));
+      mbar_arrive(RK(s));
       return true;
     };
     const uint32_t stage_w = sbase + S::OFF_P + warp * GT * 32 * 2;  // this warp's P staging
@@ -367,6 +377,7 @@ __global__ void __launch_bounds__(224, 1)
     int qf = 0;  // non-empty fragments (QR and MRG phases)
     // The unit's output row gg, dimension d = tid, value val, natural-log lse (thread 0).
     auto emit = [&](const DecodeFrag& f, size_t orow, int gg, float val, float lse) {
+      if (tid >= D) return;  // head_dim 64: threads 64..127 hold no dimension
       if (p.varlen && f.slot >= 0) {
         const size_t fs = static_cast<size_t>(f.slot) * GT + gg;  // fragment slot row
         p.o_part[fs * D + tid] = val;
@@ -409,13 +420,13 @@ __global__ void __launch_bounds__(224, 1)
         // The unit's queries, rotated at the query position into the fp16 query tile.
         const int hs = it % S::NHDR;
         ok = __all_sync(0xffffffffu, mbar_wait(HFULL(hs), (it / S::NHDR) & 1, failed, 722));
-        if (ok) {
+        if (ok && lane < GT * PAIRS) {
           const uint32_t hd = sbase + S::OFF_HDR + hs * S::HDR;
-          const int hh = lane >> 3, c = lane & 7;
+          const int hh = lane / PAIRS, c = lane % PAIRS;
           const uint4 x1 = ld_shared_v4(hd + hh * S::ROWB + c * 16);
-          const uint4 x2 = ld_shared_v4(hd + hh * S::ROWB + HALF * 2 + c * 16);
+          const uint4 x2 = ld_shared_v4(hd + hh * S::ROWB + D + c * 16);
           const uint4 cv = ld_shared_v4(hd + S::HDR_Q + c * 16);
-          const uint4 sv = ld_shared_v4(hd + S::HDR_Q + D + c * 16);
+          const uint4 sv = ld_shared_v4(hd + S::HDR_Q + S::TSPAN + c * 16);
           const uint32_t a[4] = {x1.x, x1.y, x1.z, x1.w}, bb[4] = {x2.x, x2.y, x2.z, x2.w};
           const uint32_t ca[4] = {cv.x, cv.y, cv.z, cv.w}, sa[4] = {sv.x, sv.y, sv.z, sv.w};
           uint32_t y1[4], y2[4];
@@ -427,8 +438,10 @@ __global__ void __launch_bounds__(224, 1)
             y2[e] = pack2<false>(u2.x * cc.x + u1.x * ss.x, u2.y * cc.y + u1.y * ss.y);
           }
           st_shared_v4(sbase + S::OFF_Q + swz_chunk_offset<SPAN>(NQ, hh, c), make_uint4(y1[0], y1[1], y1[2], y1[3]));
-          st_shared_v4(sbase + S::OFF_Q + swz_chunk_offset<SPAN>(NQ, hh, c + 8), make_uint4(y2[0], y2[1], y2[2], y2[3]));
+          st_shared_v4(sbase + S::OFF_Q + swz_chunk_offset<SPAN>(NQ, hh, c + PAIRS), make_uint4(y2[0], y2[1], y2[2], y2[3]));
           fence_proxy_async_smem();
+        }
+        if (ok) {
           mbar_arrive(HEMPTY(hs));
           mbar_arrive(BAR_QR);
         }
@@ -548,7 +561,7 @@ __global__ void __launch_bounds__(224, 1)
         for (int w2 = 0; w2 < 4; ++w2) {
           const float wt = ex2(mw[w2 * GT + h] - M);
           L += lw[w2 * GT + h] * wt;
-          A += mrg[(w2 * GT + h) * D + tid] * wt;
+          A += mrg[(w2 * GT + h) * D + (tid < D ? tid : 0)] * wt;
         }
         const size_t orow = static_cast<size_t>(b) * p.Hq + h0 + h;
         emit(fr, orow, h, (L > 0.f) ? A / L : 0.f,

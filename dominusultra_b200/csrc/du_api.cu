@@ -372,7 +372,7 @@ int decode_chunk_d(int GT) {
 bool decode_use_tc(int D, int GT) { return D == 128 && GT == 4; }
 
 int decode_chunk(int D, int GT, bool tc = false) {
-  if (tc && decode_use_tc(D, GT)) return du::DecodeTcShape::CK;
+  if (tc && decode_use_tc(D, GT)) return du::DecodeTcShape<128>::CK;
   switch (D) {
     case 16: return decode_chunk_d<16>(GT);
     case 32: return decode_chunk_d<32>(GT);
@@ -434,19 +434,19 @@ size_t decode_ws_bytes(const DecodePlan& pl, int B, int Hq, int D) {
   return ((o + 255) / 256) * 256 + l;
 }
 
-template <bool BF16>
+template <int D, bool BF16>
 int launch_decode_tc_t(const du::DecodeParams& prm, int B, long long rope_positions, int grid,
                        cudaStream_t st) {
-  using S = du::DecodeTcShape;
+  using S = du::DecodeTcShape<D>;
   const int dtype = BF16 ? DU_DTYPE_BF16 : DU_DTYPE_F16;
   CUtensorMap tk, tv, tc, ts;
   int rc;
   const long long units = static_cast<long long>(B) * prm.Hkv;
   if ((rc = encode_map(&tk, prm.k, dtype, S::D, prm.L, units, S::SPAN / 2, S::CK, S::SPAN)) != DU_OK) return rc;
   if ((rc = encode_map(&tv, prm.v, dtype, S::D, prm.L, units, S::SPAN / 2, S::CK, S::SPAN)) != DU_OK) return rc;
-  if ((rc = encode_map_2d_sw(&tc, prm.cos, dtype, S::D / 2, rope_positions, S::D / 2, S::CK, S::SPAN)) != DU_OK)
+  if ((rc = encode_map_2d_sw(&tc, prm.cos, dtype, S::D / 2, rope_positions, S::D / 2, S::CK, S::TSPAN)) != DU_OK)
     return rc;
-  if ((rc = encode_map_2d_sw(&ts, prm.sin, dtype, S::D / 2, rope_positions, S::D / 2, S::CK, S::SPAN)) != DU_OK)
+  if ((rc = encode_map_2d_sw(&ts, prm.sin, dtype, S::D / 2, rope_positions, S::D / 2, S::CK, S::TSPAN)) != DU_OK)
     return rc;
   auto kern = du::decode_tc_kernel<S::D, BF16, S::GT>;
   cudaError_t e = ensure_smem_attr(kern, S::SMEM_BYTES);
@@ -464,7 +464,7 @@ int launch_decode_tc_t(const du::DecodeParams& prm, int B, long long rope_positi
 template <int D, bool BF16, int GT>
 int launch_decode_split_t(const du::DecodeParams& prm, int B, long long rope_positions, int grid,
                           cudaStream_t st) {
-  if constexpr (D == 128 && GT == 4) return launch_decode_tc_t<BF16>(prm, B, rope_positions, grid, st);
+  if constexpr (D == 128 && GT == 4) return launch_decode_tc_t<D, BF16>(prm, B, rope_positions, grid, st);
   using S = du::DecodeShape<D, GT>;
   const int dtype = BF16 ? DU_DTYPE_BF16 : DU_DTYPE_F16;
   CUtensorMap tk, tv, tc, ts;
