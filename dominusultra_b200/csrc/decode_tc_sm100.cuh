@@ -1,11 +1,11 @@
-// Fused-RoPE decode for grouped-query attention on the sm_100a tensor cores: units of four query
-// heads sharing a KV head, head_dim 128 (the Llama-3-8B-shaped layer).
+// Fused-RoPE decode for grouped-query attention on the sm_100a tensor cores: units of four or
+// eight query heads sharing a KV head, head_dim 128 (the Llama-3-8B-shaped layer; group 8).
 //
 // Mathematics of the reference decode_kernel (dominus_ultra.py:288-413): per query head,
 // softmax over the cache of (R(q_pos) q) . (R(j) k_j) * scale, then the weighted sum of v_j. The
 // CUDA-core kernel (decode_sm100.cuh) spends ~70 instructions per key row on a four-head unit
 // (dot products, cross-lane reductions, P.V); here both products run on tcgen05:
-//   S^T = R(K) Q^T   M = 128 keys of a chunk, N = 16 (the unit's 4 heads, 12 zero rows), K = D.
+//   S^T = R(K) Q^T   M = 128 keys of a chunk, N = 16 (the unit's 4 or 8 heads, the rest zero), K = D.
 //                    A = the K tile as TMA left it (K-major, 128-byte swizzle), rotated in place
 //                    into fp16 by the CUDA cores; B = the unit's rotated fp16 query rows.
 //   O  += P V        M = 128 TMEM lanes (lanes 0-3 the heads, the rest zero), N = D, K = keys;
@@ -27,10 +27,10 @@
 
 namespace du {
 
-template <int D_>
+template <int D_, int GT_ = 4>
 struct DecodeTcShape {
   static constexpr int D = D_;
-  static constexpr int GT = 4;
+  static constexpr int GT = GT_;    // query heads per unit (rows of the query tile in use)
   static constexpr int NQ = 16;     // rows of the query tile (N of S^T)
   static constexpr int CK = 128;    // keys per chunk (M of S^T)
   static constexpr int SPAN = 128;  // K / V / query rows: 64-element blocks of 128 bytes
@@ -74,6 +74,7 @@ struct DecodeTcShape {
   static constexpr int TM_O = 256;  // O: D fp32 columns (lanes 32w + h: warp w's partial of head h)
   static constexpr int NTHREADS = 224;
   static_assert(D == 64 || D == 128, "tensor-core decode: head_dim 64 or 128");
+  static_assert(GT == 4 || GT == 8, "tensor-core decode: four or eight heads per unit");
   static_assert(KSTAGE % 1024 == 0 && KV_BYTES % 1024 == 0 && OFF_Q % 1024 == 0 &&
                     Q_BYTES % 1024 == 0, "swizzled tile alignment");
   static_assert(OFF_HDR % 128 == 0 && HDR % 128 == 0 && OFF_MRG % 16 == 0, "header alignment");
@@ -95,8 +96,7 @@ __global__ void __launch_bounds__(224, 1)
     decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                      const __grid_constant__ CUtensorMap tm_cos, const __grid_constant__ CUtensorMap tm_sin,
                      const DecodeParams p) {
-  using S = DecodeTcShape<D>;
-  static_assert(GT == S::GT, "tensor-core decode: four heads per unit");
+  using S = DecodeTcShape<D, GT>;
   constexpr int CK = S::CK, SPAN = S::SPAN, NQ = S::NQ, PAIRS = S::PAIRS;
   constexpr uint32_t SWZ = swizzle_code(SPAN);
   constexpr uint32_t IDESC_QK = idesc_f16(128, NQ, 0, 0, 0, 0);  // fp16 R(K) x fp16 R(Q)
@@ -420,9 +420,9 @@ __global__ void __launch_bounds__(224, 1)
         // The unit's queries, rotated at the query position into the fp16 query tile.
         const int hs = it % S::NHDR;
         ok = __all_sync(0xffffffffu, mbar_wait(HFULL(hs), (it / S::NHDR) & 1, failed, 722));
-        if (ok && lane < GT * PAIRS) {
+        for (int u = lane; ok && u < GT * PAIRS; u += 32) {
           const uint32_t hd = sbase + S::OFF_HDR + hs * S::HDR;
-          const int hh = lane / PAIRS, c = lane % PAIRS;
+          const int hh = u / PAIRS, c = u % PAIRS;
           const uint4 x1 = ld_shared_v4(hd + hh * S::ROWB + c * 16);
           const uint4 x2 = ld_shared_v4(hd + hh * S::ROWB + D + c * 16);
           const uint4 cv = ld_shared_v4(hd + S::HDR_Q + c * 16);
@@ -439,8 +439,8 @@ __global__ void __launch_bounds__(224, 1)
           }
           st_shared_v4(sbase + S::OFF_Q + swz_chunk_offset<SPAN>(NQ, hh, c), make_uint4(y1[0], y1[1], y1[2], y1[3]));
           st_shared_v4(sbase + S::OFF_Q + swz_chunk_offset<SPAN>(NQ, hh, c + PAIRS), make_uint4(y2[0], y2[1], y2[2], y2[3]));
-          fence_proxy_async_smem();
         }
+        fence_proxy_async_smem();
         if (ok) {
           mbar_arrive(HEMPTY(hs));
           mbar_arrive(BAR_QR);

@@ -367,12 +367,13 @@ int decode_chunk_d(int GT) {
   }
 }
 
-// Four-head units at head_dim 128 run on the tensor-core kernel (decode_tc_sm100.cuh), for
+// Four- and eight-head units at head_dim 128 run on the tensor-core kernel (decode_tc_sm100.cuh), for
 // du_decode, du_decode_partial and du_decode_kvcache alike.
-bool decode_use_tc(int D, int GT) { return D == 128 && GT == 4; }
+bool decode_use_tc(int D, int GT) { return D == 128 && (GT == 4 || GT == 8); }
 
 int decode_chunk(int D, int GT, bool tc = false) {
   if (tc && decode_use_tc(D, GT)) return du::DecodeTcShape<128>::CK;
+  if (GT == 8) GT = 4;  // (eight-head units exist on the tensor-core kernel only)
   switch (D) {
     case 16: return decode_chunk_d<16>(GT);
     case 32: return decode_chunk_d<32>(GT);
@@ -384,7 +385,7 @@ int decode_chunk(int D, int GT, bool tc = false) {
 
 // Resident CTAs per SM the decode kernel is built for (its launch bounds): three for one query
 // head per unit, two for two, one for four.
-int decode_residency(int GT) { return GT == 1 ? 3 : (GT == 2 ? 2 : 1); }
+int decode_residency(int GT) { return GT == 1 ? 3 : (GT == 2 ? 2 : 1); }  // 4, 8: one
 
 // Units are (b, kv head, group chunk of GT query heads). A persistent grid of resident CTAs
 // either takes whole units round-robin (when they divide evenly over the CTAs, or are so many
@@ -394,7 +395,9 @@ int decode_residency(int GT) { return GT == 1 ? 3 : (GT == 2 ? 2 : 1); }
 DecodePlan plan_decode(int B, int Hq, int Hkv, int L, int D) {
   DecodePlan pl{};
   const int G = Hq / Hkv;
-  pl.GT = (G % 4 == 0) ? 4 : ((G % 2 == 0) ? 2 : 1);
+  // Eight-head units on the tensor-core kernel read each KV byte once for groups of 8 (two
+  // four-head units read it twice: B4 H64 Hkv8 L131072 D128 measured 799 us that way).
+  pl.GT = (G % 8 == 0 && D == 128) ? 8 : (G % 4 == 0) ? 4 : ((G % 2 == 0) ? 2 : 1);
   pl.n_gchunk = G / pl.GT;
   const long long units = static_cast<long long>(B) * Hkv * pl.n_gchunk;
   const long long ctas = static_cast<long long>(sm_count()) * decode_residency(pl.GT);
@@ -434,10 +437,10 @@ size_t decode_ws_bytes(const DecodePlan& pl, int B, int Hq, int D) {
   return ((o + 255) / 256) * 256 + l;
 }
 
-template <int D, bool BF16>
+template <int D, bool BF16, int GT>
 int launch_decode_tc_t(const du::DecodeParams& prm, int B, long long rope_positions, int grid,
                        cudaStream_t st) {
-  using S = du::DecodeTcShape<D>;
+  using S = du::DecodeTcShape<D, GT>;
   const int dtype = BF16 ? DU_DTYPE_BF16 : DU_DTYPE_F16;
   CUtensorMap tk, tv, tc, ts;
   int rc;
@@ -462,9 +465,8 @@ int launch_decode_tc_t(const du::DecodeParams& prm, int B, long long rope_positi
 }
 
 template <int D, bool BF16, int GT>
-int launch_decode_split_t(const du::DecodeParams& prm, int B, long long rope_positions, int grid,
-                          cudaStream_t st) {
-  if constexpr (D == 128 && GT == 4) return launch_decode_tc_t<D, BF16>(prm, B, rope_positions, grid, st);
+int launch_decode_cuda_t(const du::DecodeParams& prm, int B, long long rope_positions, int grid,
+                         cudaStream_t st) {
   using S = du::DecodeShape<D, GT>;
   const int dtype = BF16 ? DU_DTYPE_BF16 : DU_DTYPE_F16;
   CUtensorMap tk, tv, tc, ts;
@@ -489,10 +491,25 @@ int launch_decode_split_t(const du::DecodeParams& prm, int B, long long rope_pos
   return DU_OK;
 }
 
+// The split kernel for (D, GT): tcgen05 for four- and eight-head units at head_dim 128, the
+// CUDA-core kernel otherwise.
+template <int D, bool BF16, int GT>
+int launch_decode_split_t(const du::DecodeParams& prm, int B, long long rope_positions, int grid,
+                          cudaStream_t st) {
+  if constexpr (D == 128 && (GT == 4 || GT == 8)) {
+    return launch_decode_tc_t<D, BF16, GT>(prm, B, rope_positions, grid, st);
+  } else if constexpr (GT == 8) {
+    return fail(DU_ERR_UNSUPPORTED, "eight-head decode units need head_dim 128");
+  } else {
+    return launch_decode_cuda_t<D, BF16, GT>(prm, B, rope_positions, grid, st);
+  }
+}
+
 template <int D, bool BF16>
 int launch_decode_split_g(const du::DecodeParams& prm, int GT, int B, long long rp, int grid,
                           cudaStream_t st) {
   switch (GT) {
+    case 8: return launch_decode_split_t<D, BF16, 8>(prm, B, rp, grid, st);
     case 4: return launch_decode_split_t<D, BF16, 4>(prm, B, rp, grid, st);
     case 2: return launch_decode_split_t<D, BF16, 2>(prm, B, rp, grid, st);
     default: return launch_decode_split_t<D, BF16, 1>(prm, B, rp, grid, st);

@@ -161,7 +161,7 @@ def test_decode_single_token_and_shape(cuda_device):
 
 
 TC_CASES = [
-    # B, Hq, Hkv, L, dtype: four query heads per KV head at head_dim 128 (the tcgen05 kernel)
+    # B, Hq, Hkv, L, dtype: groups of 4, 8 and 16 query heads at head_dim 128 (the tcgen05 kernel)
     (2, 8, 2, 1, torch.bfloat16),        # one key: a chunk of 128 rows with 127 masked
     (2, 8, 2, 127, torch.float16),
     (1, 16, 4, 128, torch.bfloat16),     # exactly one chunk
@@ -169,6 +169,9 @@ TC_CASES = [
     (40, 32, 8, 300, torch.bfloat16),    # 320 units: several whole units per CTA
     (2, 32, 8, 20000, torch.bfloat16),   # long split walk, fragments across units
     (1, 64, 16, 2500, torch.float16),
+    (2, 16, 2, 3000, torch.bfloat16),    # group 8: eight-head units
+    (1, 64, 4, 5000, torch.float16),     # group 16: two eight-head units per KV head
+    (24, 64, 8, 300, torch.bfloat16),    # 192 eight-head units
 ]
 
 

@@ -56,6 +56,7 @@ CASES = [
     (2, 2, 2, 100, 16, torch.float16, [40, 99]),
     (2, 4, 2, 100, 256, torch.bfloat16, [99, 1]),
     (6, 12, 4, 700, 64, torch.bfloat16, [1, 2, 3, 640, 641, 699]),  # ragged around chunks
+    (3, 16, 2, 900, 128, torch.bfloat16, [899, 5, 0]),              # group 8, an empty sequence
 ]
 
 
