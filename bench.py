@@ -18,6 +18,8 @@ sweep's largest configuration (B=8, H=Hkv=32, cache L=2048, D=64) in KV-cache HB
   (batch, kv-head) units with no communication, time = max over ranks.
 
 ``--impl reference`` times the reference's CPU path (the oracle port) on the same config.
+``--sweep`` prints one line per reference benchmark configuration instead (prefill P1-P3, the
+decode sweep P4), each graph-timed over ``--steps`` calls on rotating input sets.
 """
 
 from __future__ import annotations
@@ -503,6 +505,62 @@ def bench_ring(dist, rank, world, device, stream, steps, warmup, peaks, peak_kin
     }
 
 
+# The reference's benchmark configurations (benchmark.py sweeps): P1 its CPU-runnable case, P2
+# the MHA prefill sweep, P3 grouped- and multi-query prefill, P4 the decode sweep.
+SWEEP_PREFILL = ([("P1", dict(B=1, H=8, Hkv=8, S=512, D=64))]
+                 + [("P2", dict(B=2, H=32, Hkv=32, S=s, D=64)) for s in (128, 256, 512, 1024, 2048)]
+                 + [("P3", dict(B=2, H=32, Hkv=h, S=1024, D=64)) for h in (8, 1)])
+SWEEP_DECODE = [("P4", dict(B=8, H=32, Hkv=32, L=n, D=64)) for n in (128, 256, 512, 1024, 2048)]
+
+
+def bench_sweep(dist, rank, world, device, steps, warmup, peaks, peak_kind):
+    """One line per configuration: graph-timed device time of `steps` calls through the public
+    API, each call on a different input set (sets together > 2x L2), max over ranks."""
+    from dominusultra_b200 import dominus_ultra_decode, precompute_rope_cos_sin
+    from dominusultra_b200 import dominus_ultra_prefill
+
+    side = torch.cuda.Stream(device)
+    lines = []
+    for tag, c in SWEEP_PREFILL + SWEEP_DECODE:
+        c = dict(c, base=10000.0)
+        B, H, Hkv, D = c["B"], c["H"], c["Hkv"], c["D"]
+        prefill = "S" in c
+        n = c["S"] if prefill else c["L"]
+        per_set = (B * H * n * D + 2 * B * Hkv * n * D) * 2 if prefill else 2 * B * Hkv * n * D * 2
+        n_sets = max(2, math.ceil(2 * L2_BYTES / per_set))
+        g = torch.Generator(device=device).manual_seed(77 + rank)
+        qn = n if prefill else 1
+        sets = [tuple(torch.randn(*shape, generator=g, device=device).to(torch.bfloat16)
+                      for shape in ((B, H, qn, D), (B, Hkv, n, D), (B, Hkv, n, D)))
+                for _ in range(n_sets)]
+        cos, sin = precompute_rope_cos_sin(n if prefill else n + 1, D, device, torch.bfloat16, c["base"])
+        fn = dominus_ultra_prefill if prefill else dominus_ultra_decode
+
+        def step(i, sets=sets, cos=cos, sin=sin, fn=fn, Hkv=Hkv):
+            q, k, v = sets[i % len(sets)]
+            fn(q, k, v, cos, sin, Hkv)
+
+        for i in range(warmup):
+            step(i)
+        torch.cuda.synchronize()
+        barrier(dist)
+        ms = max_over_ranks(dist, graph_time(step, steps, side), device) / steps
+        if prefill:
+            work, unit, peak = prefill_flops(B, H, n, D) * world / 1e12, "TFLOP/s", peaks["bf16_tflops"]
+            metric, shape = "causal prefill TFLOP/s", f"prefill B{B} H{H} Hkv{Hkv} S{n} D{D}"
+        else:
+            work, unit, peak = decode_bytes(B, H, Hkv, n, D) * world / 1e9, "GB/s", peaks["hbm_gbs"]
+            metric, shape = "decode KV-cache HBM GB/s", f"decode B{B} H{H} Hkv{Hkv} L{n} D{D}"
+        value = work / (ms / 1000.0)
+        lines.append({"metric": metric, "value": value, "unit": unit, "n_gpus": world,
+                      "us_per_call": ms * 1000.0, "frac_of_peak": value / world / peak,
+                      "peak": f"{peak} {unit} per GPU ({peak_kind})", "scaling": "weak",
+                      "config": {"workload": f"{tag} {shape} bf16 RoPE base 1e4",
+                                 "l2": f"{n_sets} rotating input sets of {per_set / 1e6:.1f} MB"}})
+        del sets
+    return lines
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -516,6 +574,8 @@ def main():
     ap.add_argument("--ring", action="store_true",
                     help="only the context-parallel (ring) prefill of the Llama-3-8B-shaped layer")
     ap.add_argument("--ring-seq", type=int, default=0, help="sequence length of --ring")
+    ap.add_argument("--sweep", action="store_true",
+                    help="only the reference's benchmark configurations, one line each")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -535,6 +595,13 @@ def main():
                           peak_kind, args.ring_seq)
         if rank == 0:
             print(json.dumps(line), flush=True)
+        if dist is not None:
+            dist.destroy_process_group()
+        return 0
+    if args.sweep:
+        for line in bench_sweep(dist, rank, world, device, args.steps, args.warmup, peaks, peak_kind):
+            if rank == 0:
+                print(json.dumps(line), flush=True)
         if dist is not None:
             dist.destroy_process_group()
         return 0

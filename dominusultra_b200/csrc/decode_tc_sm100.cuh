@@ -131,12 +131,6 @@ __global__ void __launch_bounds__(224, 1)
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  if (tid == 0) griddep_launch_dependents();  // the merge may launch; it waits for completion
-
-  if (warp == 5) {
-    tmem_alloc(tmem_slot, S::TMEM_COLS);
-    tmem_relinquish();
-  }
   if (tid == 128) {
     for (int s = 0; s < S::NSTG; ++s) {
       mbar_init(FULL(s), 1);
@@ -162,14 +156,35 @@ __global__ void __launch_bounds__(224, 1)
     mbar_fence_init();
     fence_proxy_async_smem();
   }
+  // Zero the query tile (rows GT..NQ-1 stay zero).
+  if (warp < 4)
+    for (int i = tid; i < S::Q_BYTES / 16; i += 128) st_shared_v4(sbase + S::OFF_Q + 16 * i, make_uint4(0, 0, 0, 0));
+  __syncthreads();
+  // With per-sequence lengths the launch is a programmatic dependent of the prep kernel (a
+  // no-op otherwise). Everything above touches only this CTA's shared memory; once this returns
+  // the prep kernel has completed and its writes (chunk offsets, appended cache rows) are
+  // visible, including to the bulk copies (async proxy).
+  if (p.varlen) {
+    griddep_wait();
+    fence_proxy_async_global();
+  }
+  // TMEM is taken only after the wait: a CTA that held columns while waiting could starve a
+  // predecessor CTA on the same SM that has yet to allocate (tcgen05.alloc blocks).
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, S::TMEM_COLS);
+    tmem_relinquish();
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sgen + S::OFF_MISC);
+  // Dependents (the merge, or a caller's kernel launched as a programmatic dependent) may launch
+  // once every CTA of this grid holds its columns, so none of them can take the TMEM this grid
+  // still needs.
+  if (tid == 0) griddep_launch_dependents();
 
-  // Zero the query tile (rows GT..NQ-1 stay zero) and P in TMEM (lanes GT..127 stay zero).
+  // Zero P in TMEM (lanes GT..127 stay zero).
   if (warp < 4) {
-    for (int i = tid; i < S::Q_BYTES / 16; i += 128) st_shared_v4(sbase + S::OFF_Q + 16 * i, make_uint4(0, 0, 0, 0));
     const uint32_t zero[16] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
     const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
 #pragma unroll
@@ -180,13 +195,6 @@ __global__ void __launch_bounds__(224, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-
-  // Per-sequence lengths: the prep kernel (this launch's programmatic predecessor) has written
-  // the chunk offsets and the appended cache rows once this returns.
-  if (p.varlen) {
-    griddep_wait();
-    fence_proxy_async_global();  // the appended rows are read by TMA (async proxy)
-  }
 
   const uint8_t* cosb = static_cast<const uint8_t*>(p.cos);
   const uint8_t* sinb = static_cast<const uint8_t*>(p.sin);

@@ -454,10 +454,12 @@ int launch_decode_tc_t(const du::DecodeParams& prm, int B, long long rope_positi
   auto kern = du::decode_tc_kernel<S::D, BF16, S::GT>;
   cudaError_t e = ensure_smem_attr(kern, S::SMEM_BYTES);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(decode, tensor cores)");
-  // With per-sequence lengths the kernel follows decode_prep_kernel as its programmatic dependent.
+  // With per-sequence lengths the kernel follows decode_prep_kernel as its programmatic dependent
+  // (barrier set-up overlaps the prep kernel; the kernel waits before any global access and takes
+  // TMEM only after the wait). Plain decode launches are ordinary: as a dependent of the previous
+  // step its CTAs filled the free slots early and unbalanced the step (measured slower).
   e = launch_kernel(kern, dim3(static_cast<unsigned>(grid)), S::NTHREADS, S::SMEM_BYTES, st,
-                    prm.varlen != 0,
-                    tk, tv, tc, ts, prm);
+                    prm.varlen != 0, tk, tv, tc, ts, prm);
   if (e != cudaSuccess) return cuda_fail(e, "decode launch");
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "decode launch");
@@ -482,7 +484,10 @@ int launch_decode_cuda_t(const du::DecodeParams& prm, int B, long long rope_posi
   cudaError_t e = ensure_smem_attr(kern, S::SMEM_BYTES);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(decode)");
   // The work walk depends on the grid size the plan chose (resident CTAs only). With per-sequence
-  // lengths the kernel follows decode_prep_kernel as its programmatic dependent.
+  // lengths the kernel follows decode_prep_kernel as its programmatic dependent. Plain decode
+  // launches are ordinary: as a programmatic dependent of the previous step (which triggers at
+  // its start) the next step's CTAs took the free slots early and unbalanced its units
+  // (B8 H32 L2048 D64: 26.5 -> 31 us).
   e = launch_kernel(kern, static_cast<unsigned>(grid), S::NTHREADS, S::SMEM_BYTES, st,
                     prm.varlen != 0, tk, tv, tc, ts, prm);
   if (e != cudaSuccess) return cuda_fail(e, "decode launch");
