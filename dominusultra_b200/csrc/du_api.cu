@@ -279,6 +279,11 @@ int launch_prefill_t(const void* q, const void* k, const void* v, du::PrefillPar
   int rc;
   cudaError_t e;
   if constexpr (D <= 128) {
+    // Short sequences on the one-tile kernel (at most two key tiles per CTA): the attention
+    // kernel rotates its key tiles itself (at most 1.5x the rotations of a separate pass, which
+    // would cost a launch and its latency), so there is one launch.
+    using SK = du::Fa1Shape<(D <= 64) ? D : 64>;
+    const bool krot = D <= 64 && prm.T <= 2 * SK::BN;
     // 1) R(K) once per (b, kv head), fp16, into the workspace.
     du::RopeParams rp{};
     rp.x = k;
@@ -291,7 +296,7 @@ int launch_prefill_t(const void* q, const void* k, const void* v, du::PrefillPar
     rp.pos_offset = 0;
     rp.pos_split = prm.T;
     rp.pos_offset1 = 0;
-    if ((rc = launch_rope(rp, BF16, true, false, st)) != DU_OK) return rc;
+    if (!krot && (rc = launch_rope(rp, BF16, true, false, st)) != DU_OK) return rc;
     // 2) attention. Sequences up to 4096 (head_dim <= 64): one query tile per CTA, two CTAs per
     // SM, so one CTA's start-up and wind-down overlap the other's steady state (measured +3-5%
     // at S = 512-2048). Longer ones: two tiles per CTA sharing each K/V tile (+3.5% at 8192).
@@ -301,9 +306,10 @@ int launch_prefill_t(const void* q, const void* k, const void* v, du::PrefillPar
       if ((rc = encode_map(&tq, q, dtype, D, prm.T, static_cast<long long>(B) * prm.Hq, S1::SPAN / 2,
                            S1::BM, S1::SPAN)) != DU_OK)
         return rc;
-      if ((rc = encode_map(&tk, ws, DU_DTYPE_F16, D, prm.T, static_cast<long long>(B) * prm.Hkv,
-                           S1::SPAN / 2, S1::BN, S1::SPAN)) != DU_OK)
+      if ((rc = encode_map(&tk, krot ? k : ws, krot ? dtype : DU_DTYPE_F16, D, prm.T,
+                           static_cast<long long>(B) * prm.Hkv, S1::SPAN / 2, S1::BN, S1::SPAN)) != DU_OK)
         return rc;
+      prm.krot = krot ? 1 : 0;
       if ((rc = encode_map(&tv, v, dtype, D, prm.T, static_cast<long long>(B) * prm.Hkv,
                            S1::SPAN / 2, S1::BN, S1::SPAN)) != DU_OK)
         return rc;
@@ -315,7 +321,8 @@ int launch_prefill_t(const void* q, const void* k, const void* v, du::PrefillPar
       e = ensure_smem_attr(kern1, S1::SMEM_BYTES);
       if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(prefill)");
       dim3 grid1(static_cast<unsigned>(B * prm.Hq), static_cast<unsigned>(prm.n_qtiles));
-      e = launch_kernel(kern1, grid1, S1::NTHREADS, S1::SMEM_BYTES, st, true, tq, tk, tv, prm);
+      // A programmatic dependent of the rotary launch (none with krot).
+      e = launch_kernel(kern1, grid1, S1::NTHREADS, S1::SMEM_BYTES, st, !krot, tq, tk, tv, prm);
       if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
       e = cudaGetLastError();
       if (e != cudaSuccess) return cuda_fail(e, "prefill launch");

@@ -47,8 +47,8 @@ struct Fa1Shape {
   static constexpr int OFF_V = OFF_K + NSK * KV_BYTES;
   static constexpr int OFF_BAR = OFF_V + NSV * KV_BYTES;
   // barriers: q_full, q_rot, k_full[NSK], k_empty[NSK], v_full[NSV], v_empty[NSV], s_full,
-  //           s_consumed, p_full, pv_done, o_full, drain
-  static constexpr int N_BAR = 8 + 2 * NSK + 2 * NSV;
+  //           s_consumed, p_full, pv_done, o_full, drain, k_rot[NSK]
+  static constexpr int N_BAR = 8 + 3 * NSK + 2 * NSV;
   static constexpr int OFF_MISC = OFF_BAR + 8 * N_BAR;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
   static constexpr int TMEM_COLS = 256;
@@ -107,6 +107,7 @@ __global__ void __launch_bounds__(256, 2)
   const uint32_t BAR_OD = bar(XB + 3);
   const uint32_t BAR_OF = bar(XB + 4);
   const uint32_t BAR_DR = bar(XB + 5);
+  auto BAR_KR = [&](int s) { return bar(XB + 6 + s); };  // key tile rotated in place (krot)
   const uint32_t tmem_slot = sbase + S::OFF_MISC;
   volatile int* failed = reinterpret_cast<volatile int*>(sgen + S::OFF_MISC + 4);
 
@@ -132,6 +133,7 @@ __global__ void __launch_bounds__(256, 2)
     mbar_init(BAR_OD, 1);
     mbar_init(BAR_OF, 1);
     mbar_init(BAR_DR, 1);
+    for (int s = 0; s < NSK; ++s) mbar_init(BAR_KR(s), 128);
     *failed = 0;
     mbar_fence_init();
     fence_proxy_async_smem();
@@ -171,6 +173,23 @@ __global__ void __launch_bounds__(256, 2)
         if (qrow < T) rotate_row<D, BF16, SPAN, NPQ>(sbase + S::OFF_Q, BM, row, 0, 1, cv, sv);
         fence_proxy_async_smem();
         mbar_arrive(BAR_QR);
+      }
+      // Short sequences (krot: at most NSK key tiles, each in its own ring stage): the keys
+      // arrive raw and thread `row` rotates row `row` of every key tile in place into fp16, as
+      // the rotary pass would, before the first product reads it.
+      if (p.krot) {
+        for (int j = 0; ok && j < nk; ++j) {
+          const int krow = j * BN + row;
+          if (krow < T)
+            load_rope_row<NPQ>(cv, sv, cosb + static_cast<size_t>(krow) * D,
+                               sinb + static_cast<size_t>(krow) * D, 0, 1);
+          ok = __all_sync(0xffffffffu, mbar_wait(BAR_KF(j), 0, failed, 404));
+          if (!ok) break;
+          if (krow < T)
+            rotate_row<D, BF16, SPAN, NPQ>(sbase + S::OFF_K + j * S::KV_BYTES, BN, row, 0, 1, cv, sv);
+          fence_proxy_async_smem();
+          mbar_arrive(BAR_KR(j));
+        }
       }
     }
     float m = -INFINITY;
@@ -287,7 +306,8 @@ __global__ void __launch_bounds__(256, 2)
     if (lane == 0) {
       int issued = 0;
       // The rotated keys come from the preceding rotary launch (this kernel may start before
-      // it completes); nothing else this CTA reads is written by it.
+      // it completes); nothing else this CTA reads is written by it. With krot there is no such
+      // launch and the wait returns at once.
       griddep_wait();
       for (int j = 0; j < nk; ++j) {
         const int s = j % NSK;
@@ -337,6 +357,7 @@ __global__ void __launch_bounds__(256, 2)
       if (j < nk) {
         const int sk = j % NSK;
         ok = __all_sync(0xffffffffu, mbar_wait(BAR_KF(sk), (j / NSK) & 1, failed, 421));
+        if (ok && p.krot) ok = __all_sync(0xffffffffu, mbar_wait(BAR_KR(sk), 0, failed, 426));
         if (ok && j > 0) ok = __all_sync(0xffffffffu, mbar_wait(BAR_SC, (j - 1) & 1, failed, 424));
         if (!ok) break;
         tc_fence_after();

@@ -70,6 +70,9 @@ struct PrefillParams {
   float* acc_o;
   float* acc_lse;
   int acc_mode;
+  // prefill_fa1_kernel only: the K tensor map covers the raw keys and the kernel rotates each
+  // key tile in place (T <= Fa1Shape::NSK * BN, so no ring stage is reused).
+  int krot;
 };
 
 template <int D>

@@ -57,6 +57,9 @@ SMALL = [
     (2, 2, 2, 300, 128, torch.bfloat16),
     (1, 4, 4, 256, 128, torch.float16),
     (1, 2, 2, 200, 32, torch.bfloat16),
+    # the longest sequences whose key tiles the attention kernel rotates itself (two tiles)
+    (1, 4, 2, 256, 64, torch.float16),
+    (1, 2, 2, 255, 32, torch.bfloat16),
     (1, 2, 2, 150, 16, torch.bfloat16),
     (1, 2, 1, 333, 256, torch.bfloat16),
     (1, 2, 2, 128, 256, torch.float16),
