@@ -16,10 +16,18 @@ sweep's largest configuration (B=8, H=Hkv=32, cache L=2048, D=64) in KV-cache HB
   the host cores, rank 0 only.
 * Multi-GPU (torchrun): weak scaling; every rank runs the per-GPU workload on its own
   (batch, kv-head) units with no communication, time = max over ranks.
+* ``prefill_p5``: the Llama-3-8B-shaped prefill (B4 H32 Hkv8 S32768 D128) as one fixed job whose
+  32 (batch, kv-head) units are split over the ranks (strong scaling, no communication), with
+  its roofline against the sustained dense bf16 peak. ``decode_p5_shard``: the 16384-key shard
+  each rank streams in the long-context decode at eight GPUs, against the HBM peak.
+  ``decode_long``: that decode itself, the KV sequence split over the ranks, one NCCL
+  all-gather and the LSE merge per step (strong scaling).
 
 ``--impl reference`` times the reference's CPU path (the oracle port) on the same config.
 ``--sweep`` prints one line per reference benchmark configuration instead (prefill P1-P3, the
 decode sweep P4), each graph-timed over ``--steps`` calls on rotating input sets.
+``--profile-case prefill|decode NAME=VALUE ...`` runs ``--steps`` calls of one configuration
+and nothing else (the command the ncu summaries under profiles/ were taken with).
 """
 
 from __future__ import annotations
@@ -51,6 +59,25 @@ DECODE_LONG = dict(B=4, H=32, Hkv=8, L=131072, D=128, base=500000.0)
 # kernel from the ncu captures summarised under profiles/ (prefill: prefill_fa1_kernel at the
 # bench shape; decode: decode_kernel at the bench shape).
 NCU_TRAFFIC = {"prefill": 50646784 + 14848, "decode": 134576128 + 5068032}
+
+
+def headline_workload(cfg=None):
+    """The headline configuration's name, identical in both arms of the bench."""
+    c = cfg or PREFILL
+    return (f"prefill B{c['B']} H{c['H']} Hkv{c['Hkv']} S{c['S']} D{c['D']} causal RoPE base 1e4 "
+            "(per GPU)")
+
+
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+
+    return platform.processor() or "unknown"
 
 
 def prefill_flops(B, H, S, D):
@@ -311,9 +338,10 @@ def run_reference(args):
         "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1), seeded",
-        "config": {"workload": "prefill B2 H32 Hkv32 S2048 D64 causal RoPE base 1e4",
+        "config": {"workload": headline_workload(cfg),
                    "impl_path": "fp32 torch RoPE then scaled_dot_product_attention on CPU"},
-        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "cpu_model": cpu_model(),
+                         "kind": "port",
                          "sample": "full workload per step (one prefill of the config)"},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -410,6 +438,141 @@ def bench_decode_long(dist, rank, world, device, stream, steps, warmup, peaks):
                    "kv_bytes_per_gpu": total_bytes / world},
         "per_gpu_hbm_frac": (total_bytes / world) / (ms / 1000.0) / 1e9 / peaks["hbm_gbs"],
     }
+
+
+# The Llama-3-8B-shaped layer's prefill: 32 (batch, kv-head) units, split over the ranks.
+PREFILL_P5 = dict(B=4, H=32, Hkv=8, S=32768, D=128, base=500000.0)
+# What one rank streams in the long-context decode at eight GPUs: a 16384-key shard.
+DECODE_P5_SHARD = dict(B=4, H=32, Hkv=8, L=16384, D=128, base=500000.0, total=131072)
+
+
+def bench_prefill_p5(dist, rank, world, device, stream, steps, warmup, peaks, peak_kind):
+    """The fixed Llama-3-8B-shaped prefill job (B4 H32 Hkv8 S32768 D128, 35.2 TFLOP) split over
+    the ranks by ``dist.sharded_prefill``: each rank computes its contiguous range of (batch,
+    kv-head) units with no communication. Strong scaling: the job is the same at every N. Every
+    rank builds the same full inputs (one seed) and takes its slab; time = max over ranks."""
+    from dominusultra_b200 import dist as ddist
+    from dominusultra_b200 import precompute_rope_cos_sin
+
+    c = PREFILL_P5
+    B, H, Hkv, S, D = c["B"], c["H"], c["Hkv"], c["S"], c["D"]
+    g = torch.Generator(device=device).manual_seed(5500)
+    q = torch.randn(B, H, S, D, generator=g, device=device).to(torch.bfloat16)
+    k = torch.randn(B, Hkv, S, D, generator=g, device=device).to(torch.bfloat16)
+    v = torch.randn(B, Hkv, S, D, generator=g, device=device).to(torch.bfloat16)
+    cos, sin = precompute_rope_cos_sin(S, D, device, torch.bfloat16, c["base"])
+    plan = ddist.plan_prefill(B, H, Hkv, world)
+    u0, u1 = ddist.shard_range(plan.n_units, world, rank)
+    busiest = -(-plan.n_units // world)  # units of the most loaded rank
+
+    def step(_i):
+        ddist.sharded_prefill(q, k, v, cos, sin, Hkv, rank, world)
+
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    barrier(dist)
+    ms = time_region(step, steps, stream) / steps
+    ms = max_over_ranks(dist, ms, device)
+    flops = prefill_flops(B, H, S, D)
+    per_gpu = flops * busiest / plan.n_units
+    achieved = per_gpu / (ms / 1000.0) / 1e12
+    peak = peaks["bf16_tflops_sustained"]
+    return {
+        "metric": "causal prefill TFLOP/s (whole job)",
+        "value": flops / (ms / 1000.0) / 1e12, "unit": "TFLOP/s", "n_gpus": world,
+        "ms_per_step": ms, "steps": steps, "scaling": "strong",
+        "config": {"workload": f"prefill B{B} H{H} Hkv{Hkv} S{S} D{D} causal RoPE base 5e5, "
+                               f"{plan.n_units} (batch, kv-head) units sharded over {world} GPU(s) "
+                               "by dist.sharded_prefill, no communication",
+                   "units_this_rank": [u0, u1], "units_busiest_rank": busiest,
+                   "l2": "inputs 1.6 GB (> L2)"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "traffic": None,
+                     "peak_kind": f"{peak_kind} bf16 dense (sustained)",
+                     "kernel": "prefill_fa_kernel<128> (step: key rotation + attention)",
+                     "algorithmic_flops_per_gpu": per_gpu},
+    }
+
+
+def bench_decode_p5_shard(dist, rank, world, device, steps, warmup, peaks, peak_kind):
+    """One rank's share of the long-context decode at eight GPUs: decode_partial over a
+    16384-key shard (the last one: keys at positions 114688..131071, query at 131072) of
+    B4 H32 Hkv8 D128, graph-timed over two rotating input sets (268 MB each, > L2). Every rank
+    runs the same shard (weak scaling); time = max over ranks."""
+    from dominusultra_b200 import decode_partial, precompute_rope_cos_sin
+
+    c = DECODE_P5_SHARD
+    B, H, Hkv, L, D, total = c["B"], c["H"], c["Hkv"], c["L"], c["D"], c["total"]
+    off = total - L
+    g = torch.Generator(device=device).manual_seed(6000 + rank)
+    sets = [tuple(torch.randn(*shape, generator=g, device=device).to(torch.bfloat16)
+                  for shape in ((B, H, 1, D), (B, Hkv, L, D), (B, Hkv, L, D))) for _ in range(2)]
+    cos, sin = precompute_rope_cos_sin(total + 1, D, device, torch.bfloat16, c["base"])
+    o = torch.empty(B, H, D, dtype=torch.float32, device=device)
+    lse = torch.empty(B, H, dtype=torch.float32, device=device)
+
+    def step(i):
+        qq, kk, vv = sets[i % 2]
+        decode_partial(qq, kk, vv, cos, sin, Hkv, q_pos=total, kv_pos_offset=off, out=o, lse=lse)
+
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    barrier(dist)
+    side = torch.cuda.Stream(device)
+    ms = max_over_ranks(dist, graph_time(step, steps, side) / steps, device)
+    nbytes = decode_bytes(B, H, Hkv, L, D)
+    gbs = nbytes / (ms / 1000.0) / 1e9
+    from dominusultra_b200 import _lib
+
+    split = int(_lib.load().du_decode_workspace_size(B, H, Hkv, L, D)) > 0
+    return {
+        "metric": "decode KV-cache HBM GB/s per B200 (one rank's shard)",
+        "value": gbs, "unit": "GB/s", "ms_per_step": ms, "n_gpus": world, "scaling": "weak",
+        "config": {"workload": f"decode_partial B{B} H{H} Hkv{Hkv} L{L} D{D} bf16 RoPE base 5e5, "
+                               f"keys at positions {off}..{total - 1}, query at {total}",
+                   "l2": "2 rotating input sets of 268 MB (> L2)"},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": gbs / peaks["hbm_gbs"], "traffic": None,
+                     "peak_kind": f"{peak_kind} copy bandwidth",
+                     "kernel": "decode_tc_kernel<128, bf16, 4>" + (" + merge_kernel" if split else ""),
+                     "algorithmic_bytes": nbytes},
+    }
+
+
+def profile_case(args):
+    """--profile-case: a few launches of one kernel on one configuration, for ncu captures
+    (one warm-up launch, then --steps launches). Inputs are seeded N(0,1) bf16 on the device;
+    keep them above the 126 MB L2 so that DRAM counters mean something."""
+    from dominusultra_b200 import dominus_ultra_decode, dominus_ultra_prefill, precompute_rope_cos_sin
+
+    kind, sizes = args.profile_case[0], dict(kv.split("=") for kv in args.profile_case[1:])
+    B, H, Hkv, D = (int(sizes.get(n, d)) for n, d in (("B", 8), ("H", 32), ("Hkv", 32), ("D", 64)))
+    base = float(sizes.get("base", 10000.0))
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    dt = torch.bfloat16
+    if kind == "prefill":
+        S = int(sizes.get("S", 2048))
+        q = torch.randn(B, H, S, D, generator=g, device=dev).to(dt)
+        k = torch.randn(B, Hkv, S, D, generator=g, device=dev).to(dt)
+        v = torch.randn(B, Hkv, S, D, generator=g, device=dev).to(dt)
+        cos, sin = precompute_rope_cos_sin(S, D, dev, dt, base)
+        for _ in range(1 + args.steps):
+            dominus_ultra_prefill(q, k, v, cos, sin, Hkv)
+    elif kind == "decode":
+        L = int(sizes.get("L", 2048))
+        q = torch.randn(B, H, 1, D, generator=g, device=dev).to(dt)
+        k = torch.randn(B, Hkv, L, D, generator=g, device=dev).to(dt)
+        v = torch.randn(B, Hkv, L, D, generator=g, device=dev).to(dt)
+        cos, sin = precompute_rope_cos_sin(L + 1, D, dev, dt, base)
+        for _ in range(1 + args.steps):
+            dominus_ultra_decode(q, k, v, cos, sin, Hkv)
+    else:
+        raise SystemExit("--profile-case takes prefill or decode, then NAME=VALUE sizes")
+    torch.cuda.synchronize()
+    return 0
 
 
 def reference_gpu_baseline(device, steps, warmup):
@@ -576,7 +739,14 @@ def main():
     ap.add_argument("--ring-seq", type=int, default=0, help="sequence length of --ring")
     ap.add_argument("--sweep", action="store_true",
                     help="only the reference's benchmark configurations, one line each")
+    ap.add_argument("--no-p5", action="store_true",
+                    help="skip the Llama-3-8B-shaped prefill split and decode shard objects")
+    ap.add_argument("--profile-case", nargs="+", metavar="ARG",
+                    help="prefill|decode [B=.. H=.. Hkv=.. S=.. L=.. D=.. base=..]: run --steps "
+                         "launches of that call only (for ncu captures)")
     args = ap.parse_args()
+    if args.profile_case:
+        return profile_case(args)
     args.warmup = max(args.warmup, 3)
 
     if args.impl == "reference":
@@ -724,6 +894,13 @@ def main():
     if not args.no_long_decode:
         decode_long = bench_decode_long(dist, rank, world, device, stream, args.steps, args.warmup, peaks)
 
+    prefill_p5 = decode_p5_shard = None
+    if not args.no_p5:
+        prefill_p5 = bench_prefill_p5(dist, rank, world, device, stream, args.steps, args.warmup,
+                                      peaks, peak_kind)
+        decode_p5_shard = bench_decode_p5_shard(dist, rank, world, device, args.steps,
+                                                args.warmup, peaks, peak_kind)
+
     status = _lib.read_status(reset=True)
     line = None
     if rank == 0:
@@ -742,7 +919,7 @@ def main():
             "dtype": "bf16",
             "data": "synthetic N(0,1) bf16, seeded per rank; RoPE tables from precompute_rope_cos_sin",
             "config": {
-                "workload": f"prefill B{B} H{H} Hkv{Hkv} S{S} D{D} causal RoPE base 1e4 (per GPU)",
+                "workload": headline_workload(cfg),
                 "parallelism": f"(batch, kv-head) units sharded over {world} GPU(s), no communication",
                 "l2": f"{n_sets} rotating input sets of {per_set / 1e6:.0f} MB (> L2)",
             },
@@ -770,12 +947,16 @@ def main():
             line["decode"] = decode
         if decode_long is not None:
             line["decode_long"] = decode_long
+        if prefill_p5 is not None:
+            line["prefill_p5"] = prefill_p5
+        if decode_p5_shard is not None:
+            line["decode_p5_shard"] = decode_p5_shard
         if not args.no_reference_gpu:
             line["reference_gpu"] = reference_gpu_baseline(device, min(args.steps, 20), args.warmup)
         if not args.no_cpu_baseline:
             tf, t, cores = cpu_prefill_baseline(cfg)
             line["cpu_baseline"] = {
-                "value": tf, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                "value": tf, "unit": "TFLOP/s", "cores": cores, "cpu_model": cpu_model(), "kind": "port",
                 "sample": f"full workload (one prefill of the config), median of 3, {t * 1000:.0f} ms each",
             }
         print(json.dumps(line))

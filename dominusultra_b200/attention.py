@@ -165,9 +165,11 @@ class _OnDevice:
         return False
 
 
-# Decode workspace per (device, stream): reused across calls, since kernels on one stream run
-# in order; grown on demand.
+# Workspace per (kind, device, stream): [buffer, used under a graph capture], reused across
+# calls, since kernels on one stream run in order; grown on demand.
 _WORKSPACES = {}
+# Outgrown buffers that a captured CUDA graph may still reference: never freed.
+_RETIRED = []
 
 
 def dominus_ultra_prefill(
@@ -239,15 +241,28 @@ def dominus_ultra_prefill(
 
 def _cached_workspace(kind: str, nbytes: int, device, stream: int):
     """(pointer, bytes) of a per-(kind, device, stream) scratch buffer of at least nbytes, grown on
-    demand. Calls on one stream are ordered, so reusing the buffer across them is safe."""
+    demand. Calls on one stream are ordered, so reusing the buffer across them is safe.
+
+    A buffer that a CUDA graph capture has used stays referenced by that graph's kernels, so
+    when it is outgrown it is kept alive (``_RETIRED``) instead of being returned to the caching
+    allocator, where a later allocation could take the memory the graph still writes on every
+    replay. Buffers only ever used eagerly are released when outgrown (stream order makes that
+    safe). Growth is at least geometric, so few buffers are ever retired.
+    """
     if nbytes == 0:
         return 0, 0
     key = (kind, device.index, stream)
-    ws = _WORKSPACES.get(key)
-    if ws is None or ws.numel() < nbytes:
-        ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
-        _WORKSPACES[key] = ws
-    return ws.data_ptr(), ws.numel()
+    entry = _WORKSPACES.get(key)
+    capturing = torch.cuda.is_current_stream_capturing()
+    if entry is None or entry[0].numel() < nbytes:
+        if entry is not None and entry[1]:
+            _RETIRED.append(entry[0])
+        size = max(nbytes, 1 << 20, 2 * entry[0].numel() if entry is not None else 0)
+        entry = [torch.empty(size, dtype=torch.uint8, device=device), capturing]
+        _WORKSPACES[key] = entry
+    elif capturing:
+        entry[1] = True
+    return entry[0].data_ptr(), entry[0].numel()
 
 
 def _workspace(B: int, Hq: int, Hkv: int, L: int, D: int, device, stream: int):

@@ -280,8 +280,10 @@ int launch_prefill_t(const void* q, const void* k, const void* v, du::PrefillPar
   cudaError_t e;
   if constexpr (D <= 128) {
     // Short sequences on the one-tile kernel (at most two key tiles per CTA): the attention
-    // kernel rotates its key tiles itself (at most 1.5x the rotations of a separate pass, which
-    // would cost a launch and its latency), so there is one launch.
+    // kernel rotates its key tiles itself, so there is one launch instead of two. Every query
+    // head's CTAs rotate their own copy of their KV head's tiles: per query head that is at most
+    // 1.5x the rotations of a separate pass, so about 1.5 G x for a query group of G heads --
+    // a few microseconds of ALU work at these lengths against a launch and its latency saved.
     using SK = du::Fa1Shape<(D <= 64) ? D : 64>;
     const bool krot = D <= 64 && prm.T <= 2 * SK::BN;
     // 1) R(K) once per (b, kv head), fp16, into the workspace.
@@ -1031,10 +1033,42 @@ namespace {
 
 constexpr int kNoallocMaxDevices = 64;
 std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[kNoallocMaxDevices] = {};
+// Per device: the array's address and the id of the context it was looked up in. A device's
+// primary context can be destroyed and created again (cudaDeviceReset), which loads this
+// library's device image afresh, possibly at another address: the id tells the two apart.
+struct NoallocSlot {
+  unsigned long long ctx_id;
+  void* ptr;
+};
+NoallocSlot g_noalloc_slot[kNoallocMaxDevices] = {};
 
-// Device address of the scratch array on the current device, looked up on first use with that
-// device current (so the first call on a device must not happen inside a stream capture).
+// Unique id of the calling thread's current context (false if none is current or the driver
+// entry points are unavailable).
+bool current_context_id(unsigned long long* id) {
+  static PFN_cuCtxGetCurrent_v4000 get_current = nullptr;
+  static PFN_cuCtxGetId_v12000 get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(p);
+  });
+  if (get_current == nullptr || get_id == nullptr) return false;
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return false;
+  return get_id(ctx, id) == CUDA_SUCCESS;
+}
+
+// Device address of the scratch array on the current device. It is looked up with
+// cudaGetSymbolAddress (the return code checked) on the first call in each context of the
+// device, with that device current, and reused while the same context stays current; the
+// first call on a device must therefore not happen inside a stream capture.
 int noalloc_scratch_address(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -1042,13 +1076,23 @@ int noalloc_scratch_address(void** out) {
   if (dev < 0 || dev >= kNoallocMaxDevices)
     return fail(DU_ERR_UNSUPPORTED, "device index beyond the no-allocation scratch table");
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_noalloc_ptr[dev] == nullptr) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_du_noalloc_scratch);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-allocation scratch)");
-    g_noalloc_ptr[dev] = p;
+  unsigned long long id = 0;
+  NoallocSlot& slot = g_noalloc_slot[dev];
+  if (slot.ptr != nullptr && current_context_id(&id) && id == slot.ctx_id) {
+    *out = slot.ptr;
+    return DU_OK;
   }
-  *out = g_noalloc_ptr[dev];
+  void* p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_du_noalloc_scratch);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-allocation scratch)");
+  // The lookup made the device's context current; without an id the address is not cached.
+  if (current_context_id(&id)) {
+    slot.ctx_id = id;
+    slot.ptr = p;
+  } else {
+    slot.ptr = nullptr;
+  }
+  *out = p;
   return DU_OK;
 }
 

@@ -187,12 +187,17 @@ int du_merge_partials(const float* o_parts, const float* lse_parts, int R, int r
  * Same arguments, semantics and output as du_decode, minus the workspace: the split-KV
  * partials go to a fixed scratch array of DU_NOALLOC_SCRATCH_BYTES (4 MiB) compiled into this
  * library, which every GPU that loads the library holds until the process exits. Sizes whose
- * partials need more than that (see du_decode_workspace_size) are rejected with
- * DU_ERR_WORKSPACE. The first call on a device looks up that device's address of the array
- * (cudaGetSymbolAddress, with the device current); make that first call before any stream
- * capture. All calls on a device share the one array and nothing in it needs clearing (every
- * partial is written before it is read), so calls that may overlap on the GPU -- on different
- * streams, or from different host threads -- race; serialise them.
+ * partials need more than that (du_decode_workspace_size above DU_NOALLOC_SCRATCH_BYTES) are
+ * rejected with DU_ERR_WORKSPACE before anything is launched. On a 148-SM B200 every shape
+ * with head_dim <= 128, B <= 16 and Hq <= 128 fits; large batches of many heads do not
+ * (e.g. B 64, Hq 32, Hkv 8, L 8192 at head_dim 256, or B 64, Hq 128 at head_dim 128).
+ * The first call on a device, and the first after its context is re-created (for instance by
+ * cudaDeviceReset), looks up that device's address of the array (cudaGetSymbolAddress, with
+ * the device current); make that first call before any stream capture. All calls on a device
+ * share the one array and nothing in it needs clearing (every partial is written before it is
+ * read), so calls that may overlap on the GPU -- on different streams, or from different host
+ * threads -- race; serialise them. Calls issued one after the other on one stream do not
+ * overlap.
  */
 #define DU_NOALLOC_SCRATCH_BYTES (4u << 20)
 int du_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, const void* cos,

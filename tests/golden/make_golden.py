@@ -34,7 +34,7 @@ os.environ["TRITON_INTERPRET"] = "1"
 HERE = Path(__file__).resolve().parent
 
 # (B, Hq, Hkv, T, D): prefill cases, fp16. Includes GQA/MQA, T below/above and not a
-# multiple of the tile, and every head_dim the reference accepts up to 128.
+# multiple of the tile, and every head_dim the reference accepts.
 PREFILL_CASES = [
     (1, 2, 2, 64, 64),
     (1, 4, 2, 37, 64),
@@ -43,6 +43,11 @@ PREFILL_CASES = [
     (1, 2, 2, 17, 16),
     (1, 2, 2, 8, 64),
     (1, 2, 1, 1, 64),
+    # both sides of the product's switch between its one-tile (T <= 4096) and two-tile prefill
+    # kernels at head_dim 64, and head_dim 256
+    (1, 1, 1, 4096, 64),
+    (1, 1, 1, 4097, 64),
+    (1, 2, 1, 100, 256),
 ]
 # (B, Hq, Hkv, L, D): decode cases (one query at position L), fp16.
 DECODE_CASES = [
@@ -52,6 +57,7 @@ DECODE_CASES = [
     (1, 2, 2, 1, 64),
     (1, 4, 2, 200, 32),
     (1, 2, 1, 19, 16),
+    (1, 2, 1, 150, 256),
 ]
 # (positions, dim, dtype name, base): RoPE table cases.
 TABLE_CASES = [
@@ -75,7 +81,8 @@ def _np(t):
 
 def main() -> int:
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--reference", required=True,
+                        help="directory holding the reference module (dominus_ultra.py, rope.py)")
     parser.add_argument("--out", default=str(HERE / "golden.npz"))
     args = parser.parse_args()
     sys.path.insert(0, args.reference)

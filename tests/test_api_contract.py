@@ -169,6 +169,13 @@ def test_c_abi_rejects_bad_arguments_before_launch():
     assert rc == _lib.DU_ERR_INVALID and "positions" in _lib.last_error()
     rc = lib.du_merge_partials(fake, fake, 0, 4, 64, 0, 0, 0, 0, fake, _lib.DU_DTYPE_F32, null, null)
     assert rc == _lib.DU_ERR_INVALID
+    # The no-allocation decode refuses sizes beyond its fixed scratch before any CUDA call
+    # (sizes planned for 148 SMs, the B200's count and the fallback without a device).
+    need = lib.du_decode_workspace_size(64, 32, 8, 8192, 256)
+    assert need > _lib.DU_NOALLOC_SCRATCH_BYTES
+    rc = lib.du_decode_noalloc(fake, fake, fake, fake, fake, fake, 64, 32, 8, 8192, 256,
+                               _lib.DU_DTYPE_BF16, 0.0625, 8193, null)
+    assert rc == _lib.DU_ERR_WORKSPACE and str(need) in _lib.last_error()
 
 
 def test_workspace_size_is_consistent():
@@ -180,6 +187,11 @@ def test_workspace_size_is_consistent():
 
 
 def test_dropin_module_surface():
+    """Everything the reference's test file imports (test_dominus.py:16-21) is importable from
+    the same module names."""
     for name in ("precompute_rope_cos_sin", "dominus_ultra_prefill", "dominus_ultra_decode"):
         assert callable(getattr(dominus_ultra, name))
     assert callable(dominus_ultra._main)
+    import rope
+
+    assert callable(rope.make_half_split_pos_emb)

@@ -204,7 +204,7 @@ def test_kvcache_whole_units_and_split_walk_in_one_graph(cuda_device):
         with torch.cuda.graph(graph, stream=st):
             out = dominus_ultra_decode_kvcache(qd, kd, vd, cd, sd, seqlens, knd, vnd,
                                                num_kv_heads=Hkv)
-    ws = A._WORKSPACES[("decode_kvcache", torch.cuda.current_device(), st.cuda_stream)]
+    ws = A._WORKSPACES[("decode_kvcache", torch.cuda.current_device(), st.cuda_stream)][0]
     flag_at = 2 * 256  # offsets [B+1] int64 and {len, qpos} [B], each padded to 256 bytes
     kref, vref = kc.clone(), vc.clone()
     cases = [([900, 905, 890, 899, 910, 880, 902, 895], 1),

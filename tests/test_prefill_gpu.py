@@ -46,8 +46,10 @@ def _run_case(B, Hq, Hkv, T, D, dtype, seed, base=10000.0, heads=None, device="c
 
 
 SMALL = [
-    # B, Hq, Hkv, T, D, dtype
+    # B, Hq, Hkv, T, D, dtype. Head_dim <= 64 with T <= 256 takes the one-launch path whose
+    # attention kernel rotates its own key tiles (T below one 128-row key tile included).
     (1, 2, 2, 128, 64, torch.bfloat16),
+    (1, 8, 2, 64, 64, torch.bfloat16),
     (1, 2, 2, 1, 64, torch.bfloat16),
     (1, 2, 2, 8, 64, torch.bfloat16),
     (1, 2, 1, 17, 64, torch.float16),
