@@ -260,7 +260,8 @@ int launch_fa_t(const void* q, const void* k_rot, const void* v, du::PrefillPara
     return fail(DU_ERR_CUDA, "prefill kernel built with too few registers for its split");
   cudaError_t e = ensure_smem_attr(kern, S::SMEM_BYTES);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(prefill)");
-  dim3 grid(static_cast<unsigned>(B * prm.Hq), static_cast<unsigned>(prm.n_qtiles));
+  // One CTA per (query-tile pair, query head), in the kernel's group-major order.
+  dim3 grid(static_cast<unsigned>(static_cast<long long>(B) * prm.Hq * prm.n_qtiles));
   // The whole-sequence path follows its key-rotation launch as a programmatic dependent: the
   // CTAs' set-up and query loads overlap the rotation; only the K producer waits for it. The
   // block form (context-parallel prefill) is launched after arbitrary work and does not.

@@ -102,12 +102,19 @@ __global__ void __launch_bounds__(384, 1)
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const int bh = blockIdx.x;                       // b * Hq + h
-  const int pair = p.n_qtiles - 1 - blockIdx.y;    // longest first (p.n_qtiles = pair count)
-  const int b = bh / p.Hq;
-  const int h = bh - b * p.Hq;
-  const int kvh = h / (p.Hq / p.Hkv);
-  const int kv_row = b * p.Hkv + kvh;
+  // CTA order (1-D grid): KV group (b, kv head) outermost, then query-tile pairs heaviest
+  // first, then the G query heads of the group. The G CTAs that read the same K/V tiles run
+  // side by side, and a group's pairs (which read overlapping key prefixes) follow each other,
+  // so its K/V stays in L2 while it is in flight and is read from DRAM about once.
+  const int G = p.Hq / p.Hkv;
+  const int per_group = p.n_qtiles * G;          // p.n_qtiles = pair count
+  const int kv_row = static_cast<int>(blockIdx.x) / per_group;   // b * Hkv + kv head
+  const int rem = static_cast<int>(blockIdx.x) - kv_row * per_group;
+  const int pair = p.n_qtiles - 1 - rem / G;     // longest first within the group
+  const int b = kv_row / p.Hkv;
+  const int kvh = kv_row - b * p.Hkv;
+  const int h = kvh * G + (rem - (rem / G) * G);
+  const int bh = b * p.Hq + h;                   // b * Hq + h
   const int T = p.T;
   const int q_end = BLOCK ? p.q_row0 + p.Tq : T;  // query rows of this launch: [q_row0, q_end)
   const int q0a = (BLOCK ? p.q_row0 : 0) + pair * 2 * BM, q0b = q0a + BM;
