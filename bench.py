@@ -896,10 +896,11 @@ def main():
 
     prefill_p5 = decode_p5_shard = None
     if not args.no_p5:
-        prefill_p5 = bench_prefill_p5(dist, rank, world, device, stream, args.steps, args.warmup,
-                                      peaks, peak_kind)
+        # The decode shard first: the long dense prefill that follows runs at the power cap.
         decode_p5_shard = bench_decode_p5_shard(dist, rank, world, device, args.steps,
                                                 args.warmup, peaks, peak_kind)
+        prefill_p5 = bench_prefill_p5(dist, rank, world, device, stream, args.steps, args.warmup,
+                                      peaks, peak_kind)
 
     status = _lib.read_status(reset=True)
     line = None

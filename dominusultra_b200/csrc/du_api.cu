@@ -424,8 +424,23 @@ DecodePlan plan_decode(int B, int Hq, int Hkv, int L, int D) {
   // units 3 / 7 / 28 % faster whole than split; the four-head kernel (one CTA per SM) split is
   // faster at 128 and 320 units (3 / 21 %). Beyond the resident CTAs each CTA takes k units,
   // k = ceil(units / ctas), over ceil(units / k) CTAs (512 units: 31.2 -> 27.0 us).
-  const bool whole = units % ctas == 0 || units >= 8 * ctas || per < 4 ||
-                     (pl.GT <= 2 && 4 * units >= 3LL * sm_count());
+  // Few, short units (fewer than four chunks per CTA over the whole grid): fragments of at
+  // least four chunks on fewer CTAs, when that still spreads the work over more CTAs than whole
+  // units would (B1 H32 Hkv8 L4096 D128: 8 whole units on 8 CTAs took 63.5 us).
+  constexpr long long kMinPer = 4;
+  const long long short_grid = pl.total_chunks / kMinPer;
+  const bool short_split = per < kMinPer && short_grid >= 2 * units;
+  const bool whole = !short_split &&
+                     (units % ctas == 0 || units >= 8 * ctas || per < kMinPer ||
+                      (pl.GT <= 2 && 4 * units >= 3LL * sm_count()));
+  if (short_split) {
+    pl.grid = static_cast<int>(short_grid);
+    const long long sper = pl.total_chunks / short_grid;  // >= kMinPer
+    long long sslots = (pl.cpu - 1 + sper - 1) / sper + 1;
+    if (sslots < 2) sslots = 2;
+    pl.n_split = static_cast<int>(sslots);
+    return pl;
+  }
   if (whole) {
     pl.n_split = 1;
     const long long k = (units + ctas - 1) / ctas;  // units per CTA

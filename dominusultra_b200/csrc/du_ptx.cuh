@@ -474,19 +474,6 @@ __device__ __forceinline__ float2 ex2_poly2(float x0, float x1) {
                      __uint_as_float(__float_as_uint(pp.y) + (__float_as_uint(t.y) << 23)));
 }
 
-// 2^x of a packed pair of 16-bit values in the input dtype (bf16x2 or f16x2), one MUFU
-// instruction for both.
-template <bool BF16>
-__device__ __forceinline__ uint32_t ex2_x2(uint32_t x) {
-  uint32_t y;
-  if constexpr (BF16) {
-    asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(y) : "r"(x));
-  } else {
-    asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
-  }
-  return y;
-}
-
 template <bool BF16>
 __device__ __forceinline__ float2 unpack2(uint32_t w) {
   if constexpr (BF16) {

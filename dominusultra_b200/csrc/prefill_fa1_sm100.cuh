@@ -29,9 +29,6 @@
 #ifndef DU_FA1_POLY_MASK
 #define DU_FA1_POLY_MASK 0x11
 #endif
-#ifndef DU_FA1_EX2_X2
-#define DU_FA1_EX2_X2 0
-#endif
 
 namespace du {
 
@@ -243,14 +240,6 @@ __global__ void __launch_bounds__(256, 2)
 #pragma unroll
       for (int c = 0; c < BN; c += 2) {
         const float2 xx = f2_split(f2_fma(f2(s[c], s[c + 1]), SL2, NM));
-#if DU_FA1_EX2_X2
-        // The exponent rounded to the P dtype, both exponentials by one packed MUFU instruction:
-        // P comes out in the dtype the P V product takes, and the row sum adds exactly the P
-        // values that product multiplies.
-        const uint32_t pw = ex2_x2<BF16>(pack2<BF16>(xx.x, xx.y));
-        acc[(c / 2) & 3] = f2_add(acc[(c / 2) & 3], widen2<BF16>(pw));
-        pk[c / 2] = pw;
-#else
         float2 pp;
         const int q8 = (c / 2) % 8;
         if ((DU_FA1_POLY_MASK >> q8) & 1) {
@@ -260,7 +249,6 @@ __global__ void __launch_bounds__(256, 2)
         }
         acc[(c / 2) & 3] = f2_add(acc[(c / 2) & 3], f2(pp.x, pp.y));
         pk[c / 2] = pack2<BF16>(pp.x, pp.y);
-#endif
       }
       const float2 rsum = f2_split(f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3])));
       if (j > 0) {

@@ -56,15 +56,19 @@ def test_prefill_graph_replay_matches_eager(cuda_device, T, D, Hkv):
     assert_no_device_timeouts()
 
 
-@pytest.mark.parametrize("B,Hq,Hkv,L,D", [(8, 32, 32, 2048, 64), (2, 8, 2, 8192, 64), (2, 8, 2, 20000, 64),
-                                           (2, 32, 8, 3000, 128), (1, 32, 8, 131072, 128)])
-def test_decode_graph_replay_matches_eager(cuda_device, B, Hq, Hkv, L, D):
-    """Whole units (256 one-head units; four four-head units) and the split walk with its merge
-    (CUDA-core kernel at head_dim 64, tensor-core kernel at 128)."""
+@pytest.mark.parametrize("B,Hq,Hkv,L,D,split", [
+    (8, 32, 32, 2048, 64, False),   # CUDA-core kernel, 256 one-head whole units
+    (2, 8, 2, 8192, 64, True),      # CUDA-core kernel, four-head units cut into fragments
+    (2, 8, 2, 20000, 64, True),
+    (37, 16, 4, 600, 128, False),   # tensor-core kernel, 148 four-head whole units
+    (2, 32, 8, 3000, 128, True),    # tensor-core kernel, few short units over more CTAs
+    (1, 32, 8, 131072, 128, True),
+])
+def test_decode_graph_replay_matches_eager(cuda_device, B, Hq, Hkv, L, D, split):
+    """Whole units and the split walk with its merge, on both decode kernels."""
     from dominusultra_b200 import _lib
 
-    split = _lib.load().du_decode_workspace_size(B, Hq, Hkv, L, D) > 0
-    assert split == ((L, D) in ((20000, 64), (131072, 128))), "plan changed: update the cases"
+    assert (_lib.load().du_decode_workspace_size(B, Hq, Hkv, L, D) > 0) == split, "plan changed"
     dtype = torch.bfloat16
     sets = [tuple(randn(s, 90 + 3 * i + j, dtype).cuda() for j, s in
                   enumerate([(B, Hq, 1, D), (B, Hkv, L, D), (B, Hkv, L, D)])) for i in range(2)]
