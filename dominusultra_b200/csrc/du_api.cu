@@ -1147,6 +1147,11 @@ int du_trace_read(long long* out) {
   cudaError_t e = cudaMemcpyFromSymbol(out, g_du_trace, sizeof(long long) * 16 * 64);
   return e == cudaSuccess ? DU_OK : DU_ERR_CUDA;
 }
+int du_trace_reset(void) {
+  static long long zeros[16 * 64] = {};
+  cudaError_t e = cudaMemcpyToSymbol(g_du_trace, zeros, sizeof(zeros));
+  return e == cudaSuccess ? DU_OK : DU_ERR_CUDA;
+}
 #endif
 
 int du_selftest_wait_timeout(int timeout_us, void* stream) {

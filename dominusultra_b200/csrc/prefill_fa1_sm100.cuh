@@ -111,6 +111,9 @@ __global__ void __launch_bounds__(256, 2)
   const uint32_t tmem_slot = sbase + S::OFF_MISC;
   volatile int* failed = reinterpret_cast<volatile int*>(sgen + S::OFF_MISC + 4);
 
+#ifdef DU_TRACE
+  const long long t_start = clock64();
+#endif
   if (warp == 5) {
     tmem_alloc(tmem_slot, S::TMEM_COLS);
     tmem_relinquish();
@@ -195,9 +198,20 @@ __global__ void __launch_bounds__(256, 2)
     float m = -INFINITY;
     float l = 0.f;
     const uint64_t SL2 = f2(sl2, sl2);
+#ifdef DU_TRACE
+    long long t_a = clock64();
+    if (lane == 0) DU_STAT(0, t_a - t_start);
+#endif
     for (int j = 0; ok && j < nk; ++j) {
+#ifdef DU_TRACE
+      t_a = clock64();
+#endif
       ok = __all_sync(0xffffffffu, mbar_wait(BAR_SF, j & 1, failed, 401));
       if (!ok) break;
+#ifdef DU_TRACE
+      const long long t_b = clock64();
+      if (lane == 0) DU_STAT(1, t_b - t_a);
+#endif
       tc_fence_after();
       // S in two halves: the first half is masked and reduced while the second half loads.
       float s[BN];
@@ -233,6 +247,10 @@ __global__ void __launch_bounds__(256, 2)
         for (int i = 0; i < 4; ++i) mq[i] = max3(mq[i], s[c + 2 * i], s[c + 2 * i + 1]);
       }
       const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * sl2;
+#ifdef DU_TRACE
+      const long long t_c = clock64();
+      if (lane == 0) DU_STAT(2, t_c - t_b);
+#endif
       const float m_new = (mx > m + 8.0f) ? mx : m;
       const uint64_t NM = f2(-m_new, -m_new);
       uint64_t acc[4] = {f2(0.f, 0.f), f2(0.f, 0.f), f2(0.f, 0.f), f2(0.f, 0.f)};
@@ -251,6 +269,10 @@ __global__ void __launch_bounds__(256, 2)
         pk[c / 2] = pack2<BF16>(pp.x, pp.y);
       }
       const float2 rsum = f2_split(f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3])));
+#ifdef DU_TRACE
+      const long long t_d = clock64();
+      if (lane == 0) DU_STAT(3, t_d - t_c);
+#endif
       if (j > 0) {
         // PV(j-1) must be complete before P is rewritten or O rescaled.
         ok = __all_sync(0xffffffffu, mbar_wait(BAR_OD, (j - 1) & 1, failed, 403));
@@ -273,12 +295,25 @@ __global__ void __launch_bounds__(256, 2)
       }
       l += rsum.x + rsum.y;
       m = m_new;
+#ifdef DU_TRACE
+      const long long t_e = clock64();
+      if (lane == 0) DU_STAT(4, t_e - t_d);
+#endif
 #pragma unroll
       for (int c = 0; c < BN / 2; c += 16) tmem_st16u(p_addr + c, pk + c);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(BAR_PF);
+#ifdef DU_TRACE
+      if (lane == 0) {
+        DU_STAT(5, clock64() - t_e);
+        DU_STAT(6, 1);
+      }
+#endif
     }
+#ifdef DU_TRACE
+    const long long t_g = clock64();
+#endif
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(BAR_OF, 0, failed, 402));
     tc_fence_after();
     if (ok) {
@@ -300,6 +335,14 @@ __global__ void __launch_bounds__(256, 2)
       }
       if (qrow < T) p.lse[static_cast<size_t>(bh) * T + qrow] = (m + lg2(l)) * 0.69314718055994531f;
     }
+#ifdef DU_TRACE
+    if (lane == 0) {
+      const long long t_h = clock64();
+      DU_STAT(7, t_h - t_g);
+      DU_STAT(9, t_h - t_start);
+      DU_STAT(10, 1);
+    }
+#endif
   } else if (warp == 4) {
     // ------------------------------------------------------------------ TMA: the K ring
     regs_dec<S::REG_OTHER>();
@@ -356,9 +399,21 @@ __global__ void __launch_bounds__(256, 2)
     for (int j = 0; ok && j <= nk; ++j) {
       if (j < nk) {
         const int sk = j % NSK;
+#ifdef DU_TRACE
+        const long long m0 = clock64();
+#endif
         ok = __all_sync(0xffffffffu, mbar_wait(BAR_KF(sk), (j / NSK) & 1, failed, 421));
         if (ok && p.krot) ok = __all_sync(0xffffffffu, mbar_wait(BAR_KR(sk), 0, failed, 426));
+#ifdef DU_TRACE
+        const long long m1 = clock64();
+#endif
         if (ok && j > 0) ok = __all_sync(0xffffffffu, mbar_wait(BAR_SC, (j - 1) & 1, failed, 424));
+#ifdef DU_TRACE
+        if (lane == 0) {
+          DU_STAT(11, m1 - m0);
+          DU_STAT(12, clock64() - m1);
+        }
+#endif
         if (!ok) break;
         tc_fence_after();
         if (leader) {
@@ -378,8 +433,20 @@ __global__ void __launch_bounds__(256, 2)
       if (j > 0) {
         const int jv = j - 1;
         const int sv = jv % NSV;
+#ifdef DU_TRACE
+        const long long m2 = clock64();
+#endif
         ok = __all_sync(0xffffffffu, mbar_wait(BAR_PF, jv & 1, failed, 422));
+#ifdef DU_TRACE
+        const long long m3 = clock64();
+#endif
         if (ok) ok = __all_sync(0xffffffffu, mbar_wait(BAR_VF(sv), (jv / NSV) & 1, failed, 423));
+#ifdef DU_TRACE
+        if (lane == 0) {
+          DU_STAT(13, m3 - m2);
+          DU_STAT(14, clock64() - m3);
+        }
+#endif
         if (!ok) break;
         tc_fence_after();
         if (leader) {
