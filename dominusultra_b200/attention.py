@@ -258,7 +258,9 @@ def _cached_workspace(kind: str, nbytes: int, device, stream: int):
         if entry is not None and entry[1]:
             _RETIRED.append(entry[0])
         size = max(nbytes, 1 << 20, 2 * entry[0].numel() if entry is not None else 0)
-        entry = [torch.empty(size, dtype=torch.uint8, device=device), capturing]
+        # zero-filled: the decode split walk keeps its ticket counters at the front, and every
+        # call leaves them zero
+        entry = [torch.zeros(size, dtype=torch.uint8, device=device), capturing]
         _WORKSPACES[key] = entry
     elif capturing:
         entry[1] = True

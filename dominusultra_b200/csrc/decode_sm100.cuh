@@ -67,7 +67,22 @@ struct DecodeParams {
   int B;
   int ub;  // units per sequence: Hkv * n_gchunk
   int varlen;
+  // Split walk with the merge inside the split kernel (tensor-core decode, fused_merge != 0):
+  // after writing a partial, a fragment takes a ticket on unit_cnt[unit]; the fragment that
+  // completes the unit merges its rows into fin_out (fin_kind 0 fp16, 1 bf16, 2 fp32 with the
+  // natural-log lse in fin_lse). unit_cnt[DECODE_CNT_DONE] counts finished CTAs; the last one
+  // zeroes every counter, so each call leaves the counters as it found them (zero).
+  int* unit_cnt;
+  int fused_merge;
+  void* fin_out;
+  int fin_kind;
+  float* fin_lse;
 };
+
+// Workspace of the split walk: the ticket counters first (fixed size, so that calls of any
+// shape find them in the same place), then the partials.
+constexpr int DECODE_CNT_BYTES = 16384;
+constexpr int DECODE_CNT_DONE = DECODE_CNT_BYTES / 4 - 1;  // units with a fused merge: < this
 
 // Fewest chunks a CTA takes in the per-sequence-length walk: one-chunk fragments would cost
 // more in partials than they balance.

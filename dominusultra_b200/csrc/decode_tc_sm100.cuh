@@ -17,9 +17,11 @@
 // partial outputs in lanes 32w + h of O. P is double-buffered. At the end of a unit's fragment
 // the four (o, max, sum) partials are combined through shared memory.
 //
-// Warps: 0-3 rotate the K chunk one ahead, then softmax the current one (warp 0 also rotates
-// the unit's queries); 4 TMA (query header per fragment; K with the cos and sin rows of its keys
-// per chunk); 5 TMEM owner and MMA issuer; 6 TMA (V per chunk). The work walk (whole units or flattened (unit, chunk) ranges),
+// Warps: 0-3 softmax (warp 0 also rotates the unit's queries) and the per-fragment combine;
+// 4 TMA (query header per fragment; K with the cos and sin rows of its keys per chunk); 5 TMEM
+// owner and MMA issuer; 6 TMA (V per chunk); 7-10 rotate each K chunk in place as it lands, so
+// that rotation and softmax run side by side (with the four softmax warps doing both, one
+// warp per SM sub-partition streamed at most ~36 GB/s per SM). The work walk (whole units or flattened (unit, chunk) ranges),
 // partial slots and merge are those of decode_kernel. Every mbarrier wait is bounded (du_ptx.cuh).
 #pragma once
 
@@ -64,15 +66,16 @@ struct DecodeTcShape {
   static constexpr int B_FULL = 0, B_EMPTY = NSTG, B_VFULL = 2 * NSTG, B_VEMPTY = 3 * NSTG,
                        B_RK = 4 * NSTG, B_SF = 5 * NSTG, B_SC = B_SF + 1, B_OD = B_SF + 2,
                        B_PF = B_SF + 4, B_QR = B_SF + 6, B_MRG = B_SF + 7, B_HFULL = B_SF + 8,
-                       B_HEMPTY = B_SF + 10, B_DR = B_SF + 12;
-  static constexpr int N_BAR = B_DR + 1;
+                       B_HEMPTY = B_SF + 10, B_DR = B_SF + 12, B_FMA = B_SF + 13,
+                       B_FMB = B_SF + 14;
+  static constexpr int N_BAR = B_FMB + 1;
   static constexpr int OFF_MISC = OFF_BAR + 8 * N_BAR;     // tmem address, failure flag
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
   static constexpr int TMEM_COLS = 512;
   static constexpr int TM_S = 0;    // S^T: 16 fp32 columns
   static constexpr int TM_P = 64;   // P[2]: CK / 2 packed columns each
   static constexpr int TM_O = 256;  // O: D fp32 columns (lanes 32w + h: warp w's partial of head h)
-  static constexpr int NTHREADS = 224;
+  static constexpr int NTHREADS = 352;
   static_assert(D == 64 || D == 128, "tensor-core decode: head_dim 64 or 128");
   static_assert(GT == 4 || GT == 8, "tensor-core decode: four or eight heads per unit");
   static_assert(KSTAGE % 1024 == 0 && KV_BYTES % 1024 == 0 && OFF_Q % 1024 == 0 &&
@@ -92,7 +95,7 @@ __device__ __forceinline__ float pick(const float (&v)[N], int lane, float other
 }
 
 template <int D, bool BF16, int GT>
-__global__ void __launch_bounds__(224, 1)
+__global__ void __launch_bounds__(352, 1)
     decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                      const __grid_constant__ CUtensorMap tm_cos, const __grid_constant__ CUtensorMap tm_sin,
                      const DecodeParams p) {
@@ -124,6 +127,10 @@ __global__ void __launch_bounds__(224, 1)
   auto HFULL = [&](int i) { return bar(S::B_HFULL + i); };
   auto HEMPTY = [&](int i) { return bar(S::B_HEMPTY + i); };
   const uint32_t BAR_DR = bar(S::B_DR);
+  // Fused merge: every consumer thread's partial is stored and fenced (FMA); the ticket's
+  // verdict is in the shared word fm_word (FMB).
+  const uint32_t BAR_FMA = bar(S::B_FMA), BAR_FMB = bar(S::B_FMB);
+  volatile int* fm_word = reinterpret_cast<volatile int*>(sgen + S::OFF_MISC + 8);
   const uint32_t tmem_slot = sbase + S::OFF_MISC;
   volatile int* failed = reinterpret_cast<volatile int*>(sgen + S::OFF_MISC + 4);
   float* mrg = reinterpret_cast<float*>(sgen + S::OFF_MRG);  // o [4][GT][D], m [4][GT], l [4][GT]
@@ -131,6 +138,20 @@ __global__ void __launch_bounds__(224, 1)
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
+#ifdef DU_TRACE
+  // Debug-only timeline of the even CTAs (globaltimer ns): start, set-up done, first S ready,
+  // first fragment emitted, last S ready, end.
+  auto trace_ev = [&](int e) {
+    if ((blockIdx.x & 1) == 0 && blockIdx.x < 148)
+      g_du_trace[e * 74 + blockIdx.x / 2] = static_cast<long long>(globaltimer());
+  };
+  if (tid == 0) {
+    trace_ev(0);
+    uint32_t smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    if ((blockIdx.x & 1) == 0 && blockIdx.x < 148) g_du_trace[6 * 74 + blockIdx.x / 2] = smid;
+  }
+#endif
   if (tid == 128) {
     for (int s = 0; s < S::NSTG; ++s) {
       mbar_init(FULL(s), 1);
@@ -152,6 +173,8 @@ __global__ void __launch_bounds__(224, 1)
       mbar_init(HEMPTY(i), 32);
     }
     mbar_init(BAR_DR, 1);
+    mbar_init(BAR_FMA, 128);
+    mbar_init(BAR_FMB, 1);
     *failed = 0;
     mbar_fence_init();
     fence_proxy_async_smem();
@@ -198,6 +221,9 @@ __global__ void __launch_bounds__(224, 1)
 
   const uint8_t* cosb = static_cast<const uint8_t*>(p.cos);
   const uint8_t* sinb = static_cast<const uint8_t*>(p.sin);
+#ifdef DU_TRACE
+  if (tid == 0) trace_ev(1);
+#endif
 
   if (warp == 4) {
     // ------------------------------------------------------------------ TMA: headers, K + tables
@@ -338,20 +364,19 @@ __global__ void __launch_bounds__(224, 1)
       mbar_wait_drain(BAR_DR, 0, 716);
     }
     __syncwarp();
-  } else {
-    // ------------------------------------------------------------------ warps 0-3
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-    const float sl2 = p.scale_log2;
+  } else if (warp >= 7) {
+    // ------------------------------------------------------------------ warps 7-10: K rotation
     bool ok = true;
-    int g = 0, it = 0;
+    int g = 0;
     // Rotate the K tile of chunk gg in place (bf16/fp16 -> fp16 at the key positions): units
-    // (row, chunk pair), eight per thread; a quarter-warp covers one swizzled 128-byte row.
+    // (row, chunk pair), eight per thread of warps 7-10; a quarter-warp covers one swizzled
+    // 128-byte row.
     auto rotate_chunk = [&](int gg) -> bool {
       const int s = gg % S::NSTG;
       if (!__all_sync(0xffffffffu, mbar_wait(FULL(s), (gg / S::NSTG) & 1, failed, 720))) return false;
       const uint32_t st = sbase + s * S::KSTAGE;
 #pragma unroll 2
-      for (int u = tid; u < CK * PAIRS; u += 128) {
+      for (int u = tid - 224; u < CK * PAIRS; u += 128) {
         const int r = u / PAIRS, c = u % PAIRS;
         const uint32_t o1 = swz_chunk_offset<SPAN>(CK, r, c);
         const uint32_t o2 = swz_chunk_offset<SPAN>(CK, r, c + PAIRS);
@@ -377,12 +402,27 @@ __global__ void __launch_bounds__(224, 1)
       mbar_arrive(RK(s));
       return true;
     };
+    DecodeWalk walk;
+    walk.init(p);
+    DecodeFrag fr;
+    while (ok && walk.next(p, CK, fr)) {
+      const int n = (fr.kend - fr.kbeg + CK - 1) / CK;
+      for (int j = 0; ok && j < n; ++j) ok = rotate_chunk(g + j);
+      g += n;
+    }
+  } else {
+    // ------------------------------------------------------------------ warps 0-3
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const float sl2 = p.scale_log2;
+    bool ok = true;
+    int g = 0, it = 0;
     const uint32_t stage_w = sbase + S::OFF_P + warp * GT * 32 * 2;  // this warp's P staging
     uint16_t* pst = reinterpret_cast<uint16_t*>(sgen + S::OFF_P) + warp * GT * 32;
     DecodeWalk walk;
     walk.init(p);
     DecodeFrag fr;
     int qf = 0;  // non-empty fragments (QR and MRG phases)
+    int fmq = 0;  // fragments through the fused-merge ticket (FMA / FMB phases)
     // The unit's output row gg, dimension d = tid, value val, natural-log lse (thread 0).
     auto emit = [&](const DecodeFrag& f, size_t orow, int gg, float val, float lse) {
       if (tid >= D) return;  // head_dim 64: threads 64..127 hold no dimension
@@ -454,7 +494,6 @@ __global__ void __launch_bounds__(224, 1)
           mbar_arrive(BAR_QR);
         }
       }
-      if (ok) ok = rotate_chunk(g);
       // This warp's running max (log2 domain) and sum per head over its keys of the fragment.
       float m[GT], l[GT];
 #pragma unroll
@@ -464,8 +503,13 @@ __global__ void __launch_bounds__(224, 1)
       }
       for (int j = 0; ok && j < n; ++j) {
         const int gj = g + j;
-        if (j + 1 < n && !(ok = rotate_chunk(gj + 1))) break;
         if (!(ok = __all_sync(0xffffffffu, mbar_wait(BAR_SF, gj & 1, failed, 723)))) break;
+#ifdef DU_TRACE
+        if (tid == 0) {
+          if (gj == 0) trace_ev(2);
+          trace_ev(4);
+        }
+#endif
         tc_fence_after();
         float s16[16];
         tmem_ld16(tmem + lane_off + S::TM_S, s16);
@@ -575,9 +619,79 @@ __global__ void __launch_bounds__(224, 1)
         emit(fr, orow, h, (L > 0.f) ? A / L : 0.f,
              (L > 0.f) ? (M + lg2(L)) * 0.69314718055994531f : -INFINITY);
       }
+#ifdef DU_TRACE
+      if (tid == 0 && qf == 1) trace_ev(3);
+#endif
+      if (p.fused_merge && !p.varlen && fr.slot >= 0) {
+        // Ticket: the fragment that completes the unit merges its GT rows.
+        __threadfence();
+        mbar_arrive(BAR_FMA);
+        if (tid == 0) {
+          int verdict = -1;
+          if (mbar_wait(BAR_FMA, fmq & 1, failed, 729)) {
+            const long long ub = static_cast<long long>(fr.unit) * p.cpu;
+            const int nf = DecodeWalk::cta_of(p, ub + p.cpu - 1) - DecodeWalk::cta_of(p, ub) + 1;
+            verdict = (atomicAdd(&p.unit_cnt[fr.unit], 1) == nf - 1) ? nf : 0;
+          }
+          *fm_word = verdict;
+          mbar_arrive(BAR_FMB);
+        }
+        ok = __all_sync(0xffffffffu, mbar_wait(BAR_FMB, fmq & 1, failed, 730));
+        ++fmq;
+        if (!ok) break;
+        const int nf = *fm_word;
+        if (nf < 0) {
+          ok = false;
+          break;
+        }
+        if (nf > 0 && tid < D) {
+          __threadfence();  // the other fragments' partials (fenced before their tickets)
+#pragma unroll 1
+          for (int h = 0; h < GT; ++h) {
+            const size_t row = static_cast<size_t>(b) * p.Hq + h0 + h;
+            const float* lrow = p.lse_part + row * p.n_split;
+            const float* orow_p = p.o_part + row * p.n_split * D + tid;
+            float M = -INFINITY;
+            for (int sl = 0; sl < nf; ++sl) M = fmaxf(M, __ldcg(lrow + sl));
+            float L = 0.f, A = 0.f;
+            for (int sl = 0; sl < nf; ++sl) {
+              const float w = (M == -INFINITY) ? 0.f : __expf(__ldcg(lrow + sl) - M);
+              L += w;
+              A = fmaf(w, __ldcg(orow_p + static_cast<size_t>(sl) * D), A);
+            }
+            const float val = (L > 0.f) ? A / L : 0.f;
+            if (p.fin_kind == 2) {
+              static_cast<float*>(p.fin_out)[row * D + tid] = val;
+              if (tid == 0) p.fin_lse[row] = (L > 0.f) ? M + __logf(L) : -INFINITY;
+            } else if (p.fin_kind == 1) {
+              static_cast<__nv_bfloat16*>(p.fin_out)[row * D + tid] = __float2bfloat16_rn(val);
+            } else {
+              static_cast<__half*>(p.fin_out)[row * D + tid] = __float2half_rn(val);
+            }
+          }
+        }
+      }
     }
   }
 
+#ifdef DU_TRACE
+  if (tid == 0) trace_ev(5);
+#endif
+  if (p.fused_merge && !p.varlen) {
+    // The last CTA to finish zeroes the tickets for the next call (every CTA gets here, also
+    // after a failed wait, so the counters never stay dirty).
+    __syncthreads();
+    if (tid == 0) {
+      __threadfence();
+      *fm_word = (atomicAdd(&p.unit_cnt[DECODE_CNT_DONE], 1) == static_cast<int>(gridDim.x) - 1) ? 1 : 0;
+    }
+    __syncthreads();
+    if (*fm_word == 1) {
+      __threadfence();
+      for (int i = tid; i < p.n_units; i += S::NTHREADS) p.unit_cnt[i] = 0;
+      if (tid == 0) p.unit_cnt[DECODE_CNT_DONE] = 0;
+    }
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 5) {

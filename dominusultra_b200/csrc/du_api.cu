@@ -447,6 +447,22 @@ DecodePlan plan_decode(int B, int Hq, int Hkv, int L, int D) {
     pl.grid = static_cast<int>((units + k - 1) / k);
     return pl;
   }
+  // Fewer units than CTAs: k = ctas / units CTAs per unit, so that every CTA's range lies in
+  // one unit (one fragment per CTA), when that costs no more than spreading the chunks over all
+  // CTAs. A CTA whose range straddles two units finishes its first fragment, combines it and
+  // restarts its pipeline, about three chunks' time, and such CTAs set the kernel's end
+  // (measured on the tensor-core decode, B4 H32 Hkv8 D128: one fragment per CTA on 128 CTAs
+  // vs 148 CTAs, L4096 24.4 vs 29.5 us, L8192 36.8 vs 40.6, L16384 60.8 vs 61.7,
+  // L32768 109.1 vs 103.5, L131072 401 vs 384).
+  constexpr long long kFragPenalty = 3;
+  const long long k_al = units < ctas ? ctas / units : 0;
+  if (k_al >= 1 && pl.cpu >= 2 * kMinPer &&
+      (pl.cpu + k_al - 1) / k_al <= (pl.total_chunks + ctas - 1) / ctas + kFragPenalty) {
+    const long long k = k_al;
+    pl.grid = static_cast<int>(units * k);
+    pl.n_split = static_cast<int>(k);  // k == 1: whole units, final rows written directly
+    return pl;
+  }
   long long slots = (pl.cpu - 1 + per - 1) / per + 1;  // CTAs one unit's chunks can span
   if (slots < 2) slots = 2;
   pl.grid = static_cast<int>(grid);
@@ -454,12 +470,14 @@ DecodePlan plan_decode(int B, int Hq, int Hkv, int L, int D) {
   return pl;
 }
 
+// Split-walk workspace: ticket counters (du::DECODE_CNT_BYTES, zero between calls), then the
+// partials o [B * Hq, n_split, D] and lse [B * Hq, n_split] fp32.
 size_t decode_ws_bytes(const DecodePlan& pl, int B, int Hq, int D) {
   if (pl.n_split <= 1) return 0;
   const size_t rows = static_cast<size_t>(B) * Hq;
   const size_t o = rows * pl.n_split * D * sizeof(float);
   const size_t l = rows * pl.n_split * sizeof(float);
-  return ((o + 255) / 256) * 256 + l;
+  return du::DECODE_CNT_BYTES + ((o + 255) / 256) * 256 + l;
 }
 
 template <int D, bool BF16, int GT>
@@ -638,12 +656,28 @@ int decode_impl(const void* q, const void* kc, const void* vc, const void* cos, 
   if (ws == nullptr || ws_bytes < need || !aligned16(ws))
     return fail(DU_ERR_WORKSPACE, "decode workspace of " + std::to_string(need) +
                                       " bytes (16-byte aligned) is required");
-  float* o_part = static_cast<float*>(ws);
+  uint8_t* w8 = static_cast<uint8_t*>(ws);
+  float* o_part = reinterpret_cast<float*>(w8 + du::DECODE_CNT_BYTES);
   const size_t o_bytes = static_cast<size_t>(rows) * pl.n_split * D * sizeof(float);
-  float* l_part = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + ((o_bytes + 255) / 256) * 256);
+  float* l_part = reinterpret_cast<float*>(w8 + du::DECODE_CNT_BYTES + ((o_bytes + 255) / 256) * 256);
   prm.mode = 1;
   prm.o_part = o_part;
   prm.lse_part = l_part;
+  // The tensor-core decode merges in the split kernel (ticket per unit, no merge launch).
+  if (decode_use_tc(D, pl.GT) && pl.n_units < du::DECODE_CNT_DONE) {
+    prm.unit_cnt = reinterpret_cast<int*>(w8);
+    prm.fused_merge = 1;
+    if (out != nullptr) {
+      prm.fin_out = out;
+      prm.fin_kind = bf16 ? 1 : 0;
+    } else {
+      prm.fin_out = out_f32;
+      prm.fin_kind = 2;
+      prm.fin_lse = lse_f32;
+    }
+    return bf16 ? launch_decode_split_d<true>(prm, pl.GT, D, B, rope_positions, pl.grid, st)
+                : launch_decode_split_d<false>(prm, pl.GT, D, B, rope_positions, pl.grid, st);
+  }
   rc = bf16 ? launch_decode_split_d<true>(prm, pl.GT, D, B, rope_positions, pl.grid, st)
             : launch_decode_split_d<false>(prm, pl.GT, D, B, rope_positions, pl.grid, st);
   if (rc != DU_OK) return rc;

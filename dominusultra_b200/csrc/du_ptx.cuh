@@ -22,6 +22,29 @@
 //   code 6, a per-sequence cache length out of range: [1] sequence index, [2] the length.
 __device__ unsigned int g_du_status[4];
 
+#ifdef DU_TRACE
+// Debug-only (DU_TRACE builds): event timestamps of the CTA at blockIdx (0, 0) [event][tile],
+// and accumulators / per-CTA timelines recorded by the kernels.
+__device__ long long g_du_trace[16 * 64];
+#define DU_TRACE_EV(ev, j)                                                            \
+  do {                                                                               \
+    if (blockIdx.x == 0 && blockIdx.y == 0 && (j) < 64) g_du_trace[(ev) * 64 + (j)] = clock64(); \
+  } while (0)
+// Debug-only cycle accounting: slot `k` of the upper half of g_du_trace accumulates `v`.
+#define DU_STAT(k, v)                                                                          \
+  do {                                                                                         \
+    atomicAdd(reinterpret_cast<unsigned long long*>(&g_du_trace[512 + (k)]),                  \
+              static_cast<unsigned long long>(v));                                             \
+  } while (0)
+#else
+#define DU_TRACE_EV(ev, j) \
+  do {                     \
+  } while (0)
+#define DU_STAT(k, v) \
+  do {                \
+  } while (0)
+#endif
+
 namespace du {
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

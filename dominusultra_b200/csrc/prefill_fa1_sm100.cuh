@@ -29,6 +29,9 @@
 #ifndef DU_FA1_POLY_MASK
 #define DU_FA1_POLY_MASK 0x11
 #endif
+#ifndef DU_FA1_INLINE_MMA
+#define DU_FA1_INLINE_MMA 0
+#endif
 
 namespace du {
 
@@ -48,7 +51,7 @@ struct Fa1Shape {
   static constexpr int OFF_BAR = OFF_V + NSV * KV_BYTES;
   // barriers: q_full, q_rot, k_full[NSK], k_empty[NSK], v_full[NSV], v_empty[NSV], s_full,
   //           s_consumed, p_full, pv_done, o_full, drain, k_rot[NSK]
-  static constexpr int N_BAR = 8 + 3 * NSK + 2 * NSV;
+  static constexpr int N_BAR = 9 + 3 * NSK + 2 * NSV;
   static constexpr int OFF_MISC = OFF_BAR + 8 * N_BAR;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
   static constexpr int TMEM_COLS = 256;
@@ -108,6 +111,7 @@ __global__ void __launch_bounds__(256, 2)
   const uint32_t BAR_OF = bar(XB + 4);
   const uint32_t BAR_DR = bar(XB + 5);
   auto BAR_KR = [&](int s) { return bar(XB + 6 + s); };  // key tile rotated in place (krot)
+  const uint32_t BAR_DR2 = bar(XB + 6 + NSK);             // second issuer's drain
   const uint32_t tmem_slot = sbase + S::OFF_MISC;
   volatile int* failed = reinterpret_cast<volatile int*>(sgen + S::OFF_MISC + 4);
 
@@ -136,6 +140,7 @@ __global__ void __launch_bounds__(256, 2)
     mbar_init(BAR_OD, 1);
     mbar_init(BAR_OF, 1);
     mbar_init(BAR_DR, 1);
+    mbar_init(BAR_DR2, 1);
     for (int s = 0; s < NSK; ++s) mbar_init(BAR_KR(s), 128);
     *failed = 0;
     mbar_fence_init();
@@ -151,6 +156,32 @@ __global__ void __launch_bounds__(256, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sgen + S::OFF_MISC);
+  // The two products of a KV tile, issued by one thread each.
+  auto issue_qk = [&](int j) {
+    const int sk = j % NSK;
+    const uint64_t dq = smem_desc(sbase + S::OFF_Q, 16, 8 * SPAN, SWZ);
+    const uint64_t dk = smem_desc(sbase + S::OFF_K + sk * S::KV_BYTES, 16, 8 * SPAN, SWZ);
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      const uint32_t off_q = ((kk * 32) / SPAN) * BM * SPAN + (kk * 32) % SPAN;
+      const uint32_t off_k = ((kk * 32) / SPAN) * BN * SPAN + (kk * 32) % SPAN;
+      umma_f16_ss(tmem + S::TM_S, dq + (off_q >> 4), dk + (off_k >> 4), IDESC_QK, kk > 0 ? 1u : 0u);
+    }
+    umma_commit(BAR_SF);
+    umma_commit(BAR_KE(sk));
+  };
+  auto issue_pv = [&](int jv) {
+    const int sv = jv % NSV;
+    const uint64_t dv = smem_desc(sbase + S::OFF_V + sv * S::KV_BYTES, BN * SPAN, 8 * SPAN, SWZ);
+#pragma unroll
+    for (int kk = 0; kk < BN / 16; ++kk)
+      umma_f16_ts(tmem + S::TM_O, tmem + S::TM_P + kk * 8,
+                  dv + static_cast<uint64_t>((kk * 16 * SPAN) >> 4), IDESC_PV,
+                  (jv > 0 || kk > 0) ? 1u : 0u);
+    umma_commit(BAR_OD);
+    umma_commit(BAR_VE(sv));
+    if (jv == nk - 1) umma_commit(BAR_OF);
+  };
 
   if (warp < 4) {
     // ------------------------------------------------------------------ softmax
@@ -195,12 +226,31 @@ __global__ void __launch_bounds__(256, 2)
         }
       }
     }
+#if DU_FA1_INLINE_MMA
+    // Softmax threads issue the products themselves (no hand-off to an MMA warp): warp 0's
+    // first lane issues Q K^T once the key tile has landed and every thread has read the
+    // previous S; warp 1's first lane issues P V once every thread has written P.
+    const bool issuer_qk = warp == 0 && lane == 0;
+    const bool issuer_pv = warp == 1 && lane == 0;
+    if (ok) {
+      bool iok = true;
+      if (issuer_qk) {
+        iok = mbar_wait(BAR_QR, 0, failed, 430) && mbar_wait(BAR_KF(0), 0, failed, 431);
+        if (iok && p.krot) iok = mbar_wait(BAR_KR(0), 0, failed, 432);
+        if (iok) {
+          tc_fence_after();
+          issue_qk(0);
+        }
+      }
+      ok = __all_sync(0xffffffffu, iok);
+    }
+#endif
     float m = -INFINITY;
     float l = 0.f;
     const uint64_t SL2 = f2(sl2, sl2);
 #ifdef DU_TRACE
     long long t_a = clock64();
-    if (lane == 0) DU_STAT(0, t_a - t_start);
+    long long tr[8] = {t_a - t_start, 0, 0, 0, 0, 0, 0, 0};
 #endif
     for (int j = 0; ok && j < nk; ++j) {
 #ifdef DU_TRACE
@@ -210,7 +260,7 @@ __global__ void __launch_bounds__(256, 2)
       if (!ok) break;
 #ifdef DU_TRACE
       const long long t_b = clock64();
-      if (lane == 0) DU_STAT(1, t_b - t_a);
+      tr[1] += t_b - t_a;
 #endif
       tc_fence_after();
       // S in two halves: the first half is masked and reduced while the second half loads.
@@ -247,9 +297,25 @@ __global__ void __launch_bounds__(256, 2)
         for (int i = 0; i < 4; ++i) mq[i] = max3(mq[i], s[c + 2 * i], s[c + 2 * i + 1]);
       }
       const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * sl2;
+#if DU_FA1_INLINE_MMA
+      if (j + 1 < nk) {
+        bool iok = true;
+        if (issuer_qk) {
+          const int s1 = (j + 1) % NSK;
+          iok = mbar_wait(BAR_SC, j & 1, failed, 433) &&
+                mbar_wait(BAR_KF(s1), ((j + 1) / NSK) & 1, failed, 434);
+          if (iok && p.krot) iok = mbar_wait(BAR_KR(s1), 0, failed, 435);
+          if (iok) {
+            tc_fence_after();
+            issue_qk(j + 1);
+          }
+        }
+        if (!(ok = __all_sync(0xffffffffu, iok))) break;
+      }
+#endif
 #ifdef DU_TRACE
       const long long t_c = clock64();
-      if (lane == 0) DU_STAT(2, t_c - t_b);
+      tr[2] += t_c - t_b;
 #endif
       const float m_new = (mx > m + 8.0f) ? mx : m;
       const uint64_t NM = f2(-m_new, -m_new);
@@ -271,7 +337,7 @@ __global__ void __launch_bounds__(256, 2)
       const float2 rsum = f2_split(f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3])));
 #ifdef DU_TRACE
       const long long t_d = clock64();
-      if (lane == 0) DU_STAT(3, t_d - t_c);
+      tr[3] += t_d - t_c;
 #endif
       if (j > 0) {
         // PV(j-1) must be complete before P is rewritten or O rescaled.
@@ -297,18 +363,30 @@ __global__ void __launch_bounds__(256, 2)
       m = m_new;
 #ifdef DU_TRACE
       const long long t_e = clock64();
-      if (lane == 0) DU_STAT(4, t_e - t_d);
+      tr[4] += t_e - t_d;
 #endif
 #pragma unroll
       for (int c = 0; c < BN / 2; c += 16) tmem_st16u(p_addr + c, pk + c);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(BAR_PF);
-#ifdef DU_TRACE
-      if (lane == 0) {
-        DU_STAT(5, clock64() - t_e);
-        DU_STAT(6, 1);
+#if DU_FA1_INLINE_MMA
+      {
+        bool iok = true;
+        if (issuer_pv) {
+          iok = mbar_wait(BAR_PF, j & 1, failed, 436) &&
+                mbar_wait(BAR_VF(j % NSV), (j / NSV) & 1, failed, 437);
+          if (iok) {
+            tc_fence_after();
+            issue_pv(j);
+          }
+        }
+        if (!(ok = __all_sync(0xffffffffu, iok))) break;
       }
+#endif
+#ifdef DU_TRACE
+      tr[5] += clock64() - t_e;
+      tr[6] += 1;
 #endif
     }
 #ifdef DU_TRACE
@@ -335,10 +413,24 @@ __global__ void __launch_bounds__(256, 2)
       }
       if (qrow < T) p.lse[static_cast<size_t>(bh) * T + qrow] = (m + lg2(l)) * 0.69314718055994531f;
     }
+#if DU_FA1_INLINE_MMA
+    // Each issuer waits for its own products before TMEM and shared memory are released.
+    if (issuer_qk) {
+      umma_commit(BAR_DR);
+      mbar_wait_drain(BAR_DR, 0, 438);
+    }
+    if (issuer_pv) {
+      umma_commit(BAR_DR2);
+      mbar_wait_drain(BAR_DR2, 0, 439);
+    }
+    __syncwarp();
+#endif
 #ifdef DU_TRACE
     if (lane == 0) {
       const long long t_h = clock64();
-      DU_STAT(7, t_h - t_g);
+      tr[7] = t_h - t_g;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) DU_STAT(k, tr[k]);
       DU_STAT(9, t_h - t_start);
       DU_STAT(10, 1);
     }
@@ -387,13 +479,16 @@ __global__ void __launch_bounds__(256, 2)
         mbar_wait_drain(BAR_VF(j % NSV), (j / NSV) & 1, 414);
     }
     __syncwarp();
-  } else if (warp == 5) {
+  } else if (warp == 5 && !DU_FA1_INLINE_MMA) {
     // ------------------------------------------------------------------ MMA issuer
     regs_dec<S::REG_OTHER>();
     const uint64_t dq = smem_desc(sbase + S::OFF_Q, 16, 8 * SPAN, SWZ);
     const uint64_t dk0 = smem_desc(sbase + S::OFF_K, 16, 8 * SPAN, SWZ);
     const uint64_t dv0 = smem_desc(sbase + S::OFF_V, BN * SPAN, 8 * SPAN, SWZ);
     const bool leader = elect_one();
+#ifdef DU_TRACE
+    long long mt[4] = {0, 0, 0, 0};
+#endif
     bool ok = __all_sync(0xffffffffu, mbar_wait(BAR_QR, 0, failed, 420));
     // Step j: QK(j) (after the softmax has loaded S(j-1)), then PV(j-1) (once P(j-1) is in).
     for (int j = 0; ok && j <= nk; ++j) {
@@ -409,10 +504,8 @@ __global__ void __launch_bounds__(256, 2)
 #endif
         if (ok && j > 0) ok = __all_sync(0xffffffffu, mbar_wait(BAR_SC, (j - 1) & 1, failed, 424));
 #ifdef DU_TRACE
-        if (lane == 0) {
-          DU_STAT(11, m1 - m0);
-          DU_STAT(12, clock64() - m1);
-        }
+        mt[0] += m1 - m0;
+        mt[1] += clock64() - m1;
 #endif
         if (!ok) break;
         tc_fence_after();
@@ -442,10 +535,8 @@ __global__ void __launch_bounds__(256, 2)
 #endif
         if (ok) ok = __all_sync(0xffffffffu, mbar_wait(BAR_VF(sv), (jv / NSV) & 1, failed, 423));
 #ifdef DU_TRACE
-        if (lane == 0) {
-          DU_STAT(13, m3 - m2);
-          DU_STAT(14, clock64() - m3);
-        }
+        mt[2] += m3 - m2;
+        mt[3] += clock64() - m3;
 #endif
         if (!ok) break;
         tc_fence_after();
@@ -467,6 +558,10 @@ __global__ void __launch_bounds__(256, 2)
       umma_commit(BAR_DR);
       mbar_wait_drain(BAR_DR, 0, 425);
     }
+#ifdef DU_TRACE
+    if (lane == 0)
+      for (int k = 0; k < 4; ++k) DU_STAT(11 + k, mt[k]);
+#endif
     __syncwarp();
   } else {
     regs_dec<S::REG_OTHER>();

@@ -26,27 +26,6 @@
 
 #include "du_ptx.cuh"
 
-#ifdef DU_TRACE
-// Debug-only event timestamps (SM clock) of the CTA at blockIdx (0, 0): [event][tile].
-__device__ long long g_du_trace[16 * 64];
-#define DU_TRACE_EV(ev, j)                                                            \
-  do {                                                                               \
-    if (blockIdx.x == 0 && blockIdx.y == 0 && (j) < 64) g_du_trace[(ev) * 64 + (j)] = clock64(); \
-  } while (0)
-// Debug-only cycle accounting: slot `k` of the upper half of g_du_trace accumulates `v`.
-#define DU_STAT(k, v)                                                                          \
-  do {                                                                                         \
-    atomicAdd(reinterpret_cast<unsigned long long*>(&g_du_trace[512 + (k)]),                  \
-              static_cast<unsigned long long>(v));                                             \
-  } while (0)
-#else
-#define DU_TRACE_EV(ev, j) \
-  do {                     \
-  } while (0)
-#define DU_STAT(k, v) \
-  do {                \
-  } while (0)
-#endif
 
 namespace du {
 

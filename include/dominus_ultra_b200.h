@@ -109,7 +109,10 @@ int du_prefill_block(const void* q, const void* k_rot, const void* v, const void
 
 /*
  * Workspace bytes du_decode / du_decode_partial need for these sizes on the current device
- * (0 when every row's cache is handled by one CTA).
+ * (0 when every row's cache is handled by one CTA). The workspace must be zero-filled before
+ * its first use (e.g. cudaMemsetAsync once after allocating it): its first 16 KB hold the
+ * counters with which the CTAs of a split decode find the last fragment of each unit, and
+ * every call leaves them zero again, so one buffer serves any number of calls of any shape.
  */
 size_t du_decode_workspace_size(int B, int Hq, int Hkv, int L, int D);
 

@@ -131,7 +131,7 @@ def test_decode_guard_bands_untouched(cuda_device):
     lib = _lib.load()
     ws_bytes = lib.du_decode_workspace_size(B, Hq, Hkv, L, D)
     assert ws_bytes > 0  # this shape takes the multi-split path
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device="cuda")  # zero-filled before first use
     band = 2048
     n = B * Hq * D
     out_buf = torch.full((n + 2 * band,), float("nan"), dtype=dtype, device="cuda")
@@ -199,3 +199,28 @@ def test_decode_four_head_partial_outputs(cuda_device):
         ro, rl = oracle.decode_partial(q, k, v, cos, sin, Hkv, q_pos=off + L, kv_pos_offset=off)
         assert_no_device_timeouts()
         assert max_abs(o, ro) <= OUT_TOL and max_abs(lse, rl) <= LSE_TOL
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,L,D", [(4, 32, 8, 16384, 128), (1, 64, 8, 20000, 128),
+                                          (2, 32, 8, 3000, 128)])
+def test_decode_split_merge_in_kernel_leaves_counters_zero(cuda_device, B, Hq, Hkv, L, D):
+    """The tensor-core decode merges a unit's partials inside the split kernel: the CTA that
+    takes the unit's last ticket merges. Two calls in a row on one zero-filled workspace match
+    the oracle, and both leave the ticket counters (the first 16 KB) zero."""
+    lib = _lib.load()
+    ws_bytes = lib.du_decode_workspace_size(B, Hq, Hkv, L, D)
+    assert ws_bytes > 16384
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device="cuda")
+    p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for call in range(2):
+        q, k, v, cos, sin = _inputs(B, Hq, Hkv, L, D, torch.bfloat16, 6000 + 10 * call)
+        out = torch.full((B, Hq, D), float("nan"), dtype=torch.bfloat16, device="cuda")
+        dq, dk, dv, dc, ds = (t.cuda() for t in (q, k, v, cos, sin))
+        rc = lib.du_decode(p(dq), p(dk), p(dv), p(dc), p(ds), p(out), B, Hq, Hkv, L, D,
+                           _lib.DU_DTYPE_BF16, D ** -0.5, L + 1, p(ws), ws_bytes, st)
+        _lib.check(rc, "du_decode")
+        torch.cuda.synchronize()
+        assert int(ws[:16384].count_nonzero().item()) == 0, call
+        assert max_abs(out, oracle.decode(q, k, v, cos, sin, Hkv).squeeze(2)) <= OUT_TOL
+    assert_no_device_timeouts()
