@@ -330,6 +330,9 @@ __global__ void __launch_bounds__(352, 1)
       if (!ok) break;
       tc_fence_after();
       if (leader) issue_qk(g);
+#ifdef DU_TRACE
+      if (leader && g == 0) trace_ev(9);
+#endif
       __syncwarp();
       for (int j = 0; j < n; ++j) {
         const int gj = g + j;
@@ -374,6 +377,9 @@ __global__ void __launch_bounds__(352, 1)
     auto rotate_chunk = [&](int gg) -> bool {
       const int s = gg % S::NSTG;
       if (!__all_sync(0xffffffffu, mbar_wait(FULL(s), (gg / S::NSTG) & 1, failed, 720))) return false;
+#ifdef DU_TRACE
+      if (tid == 224 && gg == 0) trace_ev(7);
+#endif
       const uint32_t st = sbase + s * S::KSTAGE;
 #pragma unroll 2
       for (int u = tid - 224; u < CK * PAIRS; u += 128) {
@@ -400,6 +406,9 @@ __global__ void __launch_bounds__(352, 1)
       }
       fence_proxy_async_smem();
       mbar_arrive(RK(s));
+#ifdef DU_TRACE
+      if (tid == 224 && gg == 0) trace_ev(8);
+#endif
       return true;
     };
     DecodeWalk walk;
@@ -623,15 +632,19 @@ __global__ void __launch_bounds__(352, 1)
       if (tid == 0 && qf == 1) trace_ev(3);
 #endif
       if (p.fused_merge && !p.varlen && fr.slot >= 0) {
-        // Ticket: the fragment that completes the unit merges its GT rows.
-        __threadfence();
+        // Ticket: the fragment that completes the unit merges its GT rows. The consumer threads'
+        // partial stores reach thread 0 through the barrier (release / acquire in the CTA); its
+        // fence makes them visible device-wide before the ticket, and after the last ticket
+        // makes the other fragments' partials visible to this CTA.
         mbar_arrive(BAR_FMA);
         if (tid == 0) {
           int verdict = -1;
           if (mbar_wait(BAR_FMA, fmq & 1, failed, 729)) {
+            __threadfence();
             const long long ub = static_cast<long long>(fr.unit) * p.cpu;
             const int nf = DecodeWalk::cta_of(p, ub + p.cpu - 1) - DecodeWalk::cta_of(p, ub) + 1;
             verdict = (atomicAdd(&p.unit_cnt[fr.unit], 1) == nf - 1) ? nf : 0;
+            if (verdict > 0) __threadfence();
           }
           *fm_word = verdict;
           mbar_arrive(BAR_FMB);
@@ -645,24 +658,54 @@ __global__ void __launch_bounds__(352, 1)
           break;
         }
         if (nf > 0 && tid < D) {
-          __threadfence();  // the other fragments' partials (fenced before their tickets)
-#pragma unroll 1
+          // Online LSE merge of the nf partials of each head, NB slots per batch of loads (all
+          // of a batch's loads in flight at once: one L2 round trip per batch).
+          constexpr int NB = 32 / GT;
+          float M[GT], L[GT], A[GT];
+#pragma unroll
           for (int h = 0; h < GT; ++h) {
-            const size_t row = static_cast<size_t>(b) * p.Hq + h0 + h;
-            const float* lrow = p.lse_part + row * p.n_split;
-            const float* orow_p = p.o_part + row * p.n_split * D + tid;
-            float M = -INFINITY;
-            for (int sl = 0; sl < nf; ++sl) M = fmaxf(M, __ldcg(lrow + sl));
-            float L = 0.f, A = 0.f;
-            for (int sl = 0; sl < nf; ++sl) {
-              const float w = (M == -INFINITY) ? 0.f : __expf(__ldcg(lrow + sl) - M);
-              L += w;
-              A = fmaf(w, __ldcg(orow_p + static_cast<size_t>(sl) * D), A);
+            M[h] = -INFINITY;
+            L[h] = 0.f;
+            A[h] = 0.f;
+          }
+          const size_t row0 = static_cast<size_t>(b) * p.Hq + h0;
+#pragma unroll 1
+          for (int s0 = 0; s0 < nf; s0 += NB) {
+            float lv[GT][NB], ov[GT][NB];
+#pragma unroll
+            for (int h = 0; h < GT; ++h)
+#pragma unroll
+              for (int i = 0; i < NB; ++i) {
+                const bool in = s0 + i < nf;
+                const size_t sr = (row0 + h) * p.n_split + s0 + i;
+                lv[h][i] = in ? __ldcg(p.lse_part + sr) : -INFINITY;
+                ov[h][i] = in ? __ldcg(p.o_part + sr * D + tid) : 0.f;
+              }
+#pragma unroll
+            for (int h = 0; h < GT; ++h) {
+              float mb = M[h];
+#pragma unroll
+              for (int i = 0; i < NB; ++i) mb = fmaxf(mb, lv[h][i]);
+              if (mb == -INFINITY) continue;
+              const float sc = __expf(M[h] - mb);
+              L[h] *= sc;
+              A[h] *= sc;
+#pragma unroll
+              for (int i = 0; i < NB; ++i) {
+                const float w = __expf(lv[h][i] - mb);
+                L[h] += w;
+                A[h] = fmaf(w, ov[h][i], A[h]);
+              }
+              M[h] = mb;
             }
-            const float val = (L > 0.f) ? A / L : 0.f;
+          }
+#pragma unroll
+          for (int h = 0; h < GT; ++h) {
+            const size_t row = row0 + h;
+            const float val = (L[h] > 0.f) ? A[h] / L[h] : 0.f;
             if (p.fin_kind == 2) {
               static_cast<float*>(p.fin_out)[row * D + tid] = val;
-              if (tid == 0) p.fin_lse[row] = (L > 0.f) ? M + __logf(L) : -INFINITY;
+              if (tid == 0) p.fin_lse[row] = (L[h] > 0.f) ? M[h] + __logf(L[h]) : -INFINITY;
             } else if (p.fin_kind == 1) {
               static_cast<__nv_bfloat16*>(p.fin_out)[row * D + tid] = __float2bfloat16_rn(val);
             } else {
