@@ -345,7 +345,7 @@ def run_reference(args):
                          "sample": "full workload per step (one prefill of the config)"},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line))
+    print(json.dumps(line), flush=True)
     return 0
 
 
@@ -960,7 +960,7 @@ def main():
                 "value": tf, "unit": "TFLOP/s", "cores": cores, "cpu_model": cpu_model(), "kind": "port",
                 "sample": f"full workload (one prefill of the config), median of 3, {t * 1000:.0f} ms each",
             }
-        print(json.dumps(line))
+        print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()

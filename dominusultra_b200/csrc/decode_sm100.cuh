@@ -304,6 +304,15 @@ __global__ void __launch_bounds__(DecodeShape<D, GT>::NTHREADS, (GT == 1) ? 3 : 
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+#ifdef DU_TRACE
+  // Debug-only timeline of the even CTAs below 148 (globaltimer ns): start, set-up done, first
+  // chunk landed (consumer warp 0), end.
+  auto trace_ev = [&](int e) {
+    if ((blockIdx.x & 1) == 0 && blockIdx.x < 148)
+      g_du_trace[e * 74 + blockIdx.x / 2] = static_cast<long long>(globaltimer());
+  };
+  if (threadIdx.x == 0) trace_ev(0);
+#endif
   // The merge launched after this kernel may start its launch now; it waits for our completion.
   if (threadIdx.x == 0) griddep_launch_dependents();
   if (threadIdx.x == 0) {
@@ -331,6 +340,9 @@ __global__ void __launch_bounds__(DecodeShape<D, GT>::NTHREADS, (GT == 1) ? 3 : 
 
   const uint8_t* cosb = static_cast<const uint8_t*>(p.cos);
   const uint8_t* sinb = static_cast<const uint8_t*>(p.sin);
+#ifdef DU_TRACE
+  if (threadIdx.x == 0) trace_ev(1);
+#endif
 
   if (warp == S::NW) {
     // ------------------------------------------------------------------ bulk-copy producer
@@ -475,6 +487,9 @@ __global__ void __launch_bounds__(DecodeShape<D, GT>::NTHREADS, (GT == 1) ? 3 : 
         ok = false;
         break;
       }
+#ifdef DU_TRACE
+      if (threadIdx.x == 0 && g == 0) trace_ev(2);
+#endif
       const int n = min(CK, kend - c0);
       const uint32_t st = sbase + s * S::STAGE;
       float sc[S::STEPS][GT];
@@ -663,6 +678,9 @@ __global__ void __launch_bounds__(DecodeShape<D, GT>::NTHREADS, (GT == 1) ? 3 : 
     ok = mbar_wait(MERGE(1), it & 1, failed, 64);
     if (!__all_sync(0xffffffffu, ok)) break;
   }
+#ifdef DU_TRACE
+  if (threadIdx.x == 0) trace_ev(5);
+#endif
 }
 
 constexpr int MERGE_MAX_R = 4096;

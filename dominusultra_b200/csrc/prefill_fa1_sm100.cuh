@@ -29,9 +29,6 @@
 #ifndef DU_FA1_POLY_MASK
 #define DU_FA1_POLY_MASK 0x11
 #endif
-#ifndef DU_FA1_INLINE_MMA
-#define DU_FA1_INLINE_MMA 0
-#endif
 
 namespace du {
 
@@ -51,7 +48,7 @@ struct Fa1Shape {
   static constexpr int OFF_BAR = OFF_V + NSV * KV_BYTES;
   // barriers: q_full, q_rot, k_full[NSK], k_empty[NSK], v_full[NSV], v_empty[NSV], s_full,
   //           s_consumed, p_full, pv_done, o_full, drain, k_rot[NSK]
-  static constexpr int N_BAR = 9 + 3 * NSK + 2 * NSV;
+  static constexpr int N_BAR = 8 + 3 * NSK + 2 * NSV;
   static constexpr int OFF_MISC = OFF_BAR + 8 * N_BAR;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
   static constexpr int TMEM_COLS = 256;
@@ -111,12 +108,14 @@ __global__ void __launch_bounds__(256, 2)
   const uint32_t BAR_OF = bar(XB + 4);
   const uint32_t BAR_DR = bar(XB + 5);
   auto BAR_KR = [&](int s) { return bar(XB + 6 + s); };  // key tile rotated in place (krot)
-  const uint32_t BAR_DR2 = bar(XB + 6 + NSK);             // second issuer's drain
   const uint32_t tmem_slot = sbase + S::OFF_MISC;
   volatile int* failed = reinterpret_cast<volatile int*>(sgen + S::OFF_MISC + 4);
 
 #ifdef DU_TRACE
   const long long t_start = clock64();
+#endif
+#ifdef DU_TRACE_SM0
+  const long long t_entry = clock64();
 #endif
   if (warp == 5) {
     tmem_alloc(tmem_slot, S::TMEM_COLS);
@@ -140,7 +139,6 @@ __global__ void __launch_bounds__(256, 2)
     mbar_init(BAR_OD, 1);
     mbar_init(BAR_OF, 1);
     mbar_init(BAR_DR, 1);
-    mbar_init(BAR_DR2, 1);
     for (int s = 0; s < NSK; ++s) mbar_init(BAR_KR(s), 128);
     *failed = 0;
     mbar_fence_init();
@@ -156,32 +154,6 @@ __global__ void __launch_bounds__(256, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sgen + S::OFF_MISC);
-  // The two products of a KV tile, issued by one thread each.
-  auto issue_qk = [&](int j) {
-    const int sk = j % NSK;
-    const uint64_t dq = smem_desc(sbase + S::OFF_Q, 16, 8 * SPAN, SWZ);
-    const uint64_t dk = smem_desc(sbase + S::OFF_K + sk * S::KV_BYTES, 16, 8 * SPAN, SWZ);
-#pragma unroll
-    for (int kk = 0; kk < D / 16; ++kk) {
-      const uint32_t off_q = ((kk * 32) / SPAN) * BM * SPAN + (kk * 32) % SPAN;
-      const uint32_t off_k = ((kk * 32) / SPAN) * BN * SPAN + (kk * 32) % SPAN;
-      umma_f16_ss(tmem + S::TM_S, dq + (off_q >> 4), dk + (off_k >> 4), IDESC_QK, kk > 0 ? 1u : 0u);
-    }
-    umma_commit(BAR_SF);
-    umma_commit(BAR_KE(sk));
-  };
-  auto issue_pv = [&](int jv) {
-    const int sv = jv % NSV;
-    const uint64_t dv = smem_desc(sbase + S::OFF_V + sv * S::KV_BYTES, BN * SPAN, 8 * SPAN, SWZ);
-#pragma unroll
-    for (int kk = 0; kk < BN / 16; ++kk)
-      umma_f16_ts(tmem + S::TM_O, tmem + S::TM_P + kk * 8,
-                  dv + static_cast<uint64_t>((kk * 16 * SPAN) >> 4), IDESC_PV,
-                  (jv > 0 || kk > 0) ? 1u : 0u);
-    umma_commit(BAR_OD);
-    umma_commit(BAR_VE(sv));
-    if (jv == nk - 1) umma_commit(BAR_OF);
-  };
 
   if (warp < 4) {
     // ------------------------------------------------------------------ softmax
@@ -226,28 +198,27 @@ __global__ void __launch_bounds__(256, 2)
         }
       }
     }
-#if DU_FA1_INLINE_MMA
-    // Softmax threads issue the products themselves (no hand-off to an MMA warp): warp 0's
-    // first lane issues Q K^T once the key tile has landed and every thread has read the
-    // previous S; warp 1's first lane issues P V once every thread has written P.
-    const bool issuer_qk = warp == 0 && lane == 0;
-    const bool issuer_pv = warp == 1 && lane == 0;
-    if (ok) {
-      bool iok = true;
-      if (issuer_qk) {
-        iok = mbar_wait(BAR_QR, 0, failed, 430) && mbar_wait(BAR_KF(0), 0, failed, 431);
-        if (iok && p.krot) iok = mbar_wait(BAR_KR(0), 0, failed, 432);
-        if (iok) {
-          tc_fence_after();
-          issue_qk(0);
-        }
-      }
-      ok = __all_sync(0xffffffffu, iok);
-    }
-#endif
     float m = -INFINITY;
     float l = 0.f;
     const uint64_t SL2 = f2(sl2, sl2);
+#ifdef DU_TRACE_SM0
+    // Debug-only timeline of the CTAs on SM 0 (softmax warp 0): [slot][tile] exp start / end.
+    int t0slot = -1;
+    if (tid == 0) {
+      uint32_t smid;
+      asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+      if (smid == 0) {
+        t0slot = static_cast<int>(atomicAdd(reinterpret_cast<unsigned long long*>(&g_du_trace[1000]), 1ull));
+        if (t0slot < 18) {
+          g_du_trace[t0slot * 50 + 0] = clock64();
+          g_du_trace[t0slot * 50 + 1] = nk;
+          g_du_trace[t0slot * 50 + 48] = t_entry;
+        } else {
+          t0slot = -1;
+        }
+      }
+    }
+#endif
 #ifdef DU_TRACE
     long long t_a = clock64();
     long long tr[8] = {t_a - t_start, 0, 0, 0, 0, 0, 0, 0};
@@ -297,28 +268,15 @@ __global__ void __launch_bounds__(256, 2)
         for (int i = 0; i < 4; ++i) mq[i] = max3(mq[i], s[c + 2 * i], s[c + 2 * i + 1]);
       }
       const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * sl2;
-#if DU_FA1_INLINE_MMA
-      if (j + 1 < nk) {
-        bool iok = true;
-        if (issuer_qk) {
-          const int s1 = (j + 1) % NSK;
-          iok = mbar_wait(BAR_SC, j & 1, failed, 433) &&
-                mbar_wait(BAR_KF(s1), ((j + 1) / NSK) & 1, failed, 434);
-          if (iok && p.krot) iok = mbar_wait(BAR_KR(s1), 0, failed, 435);
-          if (iok) {
-            tc_fence_after();
-            issue_qk(j + 1);
-          }
-        }
-        if (!(ok = __all_sync(0xffffffffu, iok))) break;
-      }
-#endif
 #ifdef DU_TRACE
       const long long t_c = clock64();
       tr[2] += t_c - t_b;
 #endif
       const float m_new = (mx > m + 8.0f) ? mx : m;
       const uint64_t NM = f2(-m_new, -m_new);
+#ifdef DU_TRACE_SM0
+      if (t0slot >= 0 && j < 16) g_du_trace[t0slot * 50 + 2 + 3 * j] = clock64();
+#endif
       uint64_t acc[4] = {f2(0.f, 0.f), f2(0.f, 0.f), f2(0.f, 0.f), f2(0.f, 0.f)};
       uint32_t pk[BN / 2];
 #pragma unroll
@@ -335,6 +293,9 @@ __global__ void __launch_bounds__(256, 2)
         pk[c / 2] = pack2<BF16>(pp.x, pp.y);
       }
       const float2 rsum = f2_split(f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3])));
+#ifdef DU_TRACE_SM0
+      if (t0slot >= 0 && j < 16) g_du_trace[t0slot * 50 + 3 + 3 * j] = clock64();
+#endif
 #ifdef DU_TRACE
       const long long t_d = clock64();
       tr[3] += t_d - t_c;
@@ -370,19 +331,8 @@ __global__ void __launch_bounds__(256, 2)
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(BAR_PF);
-#if DU_FA1_INLINE_MMA
-      {
-        bool iok = true;
-        if (issuer_pv) {
-          iok = mbar_wait(BAR_PF, j & 1, failed, 436) &&
-                mbar_wait(BAR_VF(j % NSV), (j / NSV) & 1, failed, 437);
-          if (iok) {
-            tc_fence_after();
-            issue_pv(j);
-          }
-        }
-        if (!(ok = __all_sync(0xffffffffu, iok))) break;
-      }
+#ifdef DU_TRACE_SM0
+      if (t0slot >= 0 && j < 16) g_du_trace[t0slot * 50 + 4 + 3 * j] = clock64();
 #endif
 #ifdef DU_TRACE
       tr[5] += clock64() - t_e;
@@ -413,17 +363,8 @@ __global__ void __launch_bounds__(256, 2)
       }
       if (qrow < T) p.lse[static_cast<size_t>(bh) * T + qrow] = (m + lg2(l)) * 0.69314718055994531f;
     }
-#if DU_FA1_INLINE_MMA
-    // Each issuer waits for its own products before TMEM and shared memory are released.
-    if (issuer_qk) {
-      umma_commit(BAR_DR);
-      mbar_wait_drain(BAR_DR, 0, 438);
-    }
-    if (issuer_pv) {
-      umma_commit(BAR_DR2);
-      mbar_wait_drain(BAR_DR2, 0, 439);
-    }
-    __syncwarp();
+#ifdef DU_TRACE_SM0
+    if (t0slot >= 0) g_du_trace[t0slot * 50 + 49] = clock64();
 #endif
 #ifdef DU_TRACE
     if (lane == 0) {
@@ -479,7 +420,7 @@ __global__ void __launch_bounds__(256, 2)
         mbar_wait_drain(BAR_VF(j % NSV), (j / NSV) & 1, 414);
     }
     __syncwarp();
-  } else if (warp == 5 && !DU_FA1_INLINE_MMA) {
+  } else if (warp == 5) {
     // ------------------------------------------------------------------ MMA issuer
     regs_dec<S::REG_OTHER>();
     const uint64_t dq = smem_desc(sbase + S::OFF_Q, 16, 8 * SPAN, SWZ);
