@@ -315,7 +315,46 @@ __global__ void __launch_bounds__(DecodeShape<D, GT>::NTHREADS, (GT == 1) ? 3 : 
 #endif
   // The merge launched after this kernel may start its launch now; it waits for our completion.
   if (threadIdx.x == 0) griddep_launch_dependents();
-  if (threadIdx.x == 0) {
+  const uint8_t* cosb = static_cast<const uint8_t*>(p.cos);
+  const uint8_t* sinb = static_cast<const uint8_t*>(p.sin);
+  // Item header: query rows of the GT heads and the cos / sin rows at the query position, into
+  // header slot hs (producer thread).
+  auto issue_header = [&](const DecodeFrag& f, int hs) {
+    const int gch = f.unit % p.n_gchunk;
+    const int bk = f.unit / p.n_gchunk;  // b * Hkv + kvh
+    const int b = bk / p.Hkv;
+    const int h0 = (bk - b * p.Hkv) * p.G + gch * GT;
+    const uint32_t hd = sbase + S::OFF_HDR + hs * S::HDR;
+    const size_t trow = static_cast<size_t>(f.qpos) * S::TABB;
+    mbar_expect_tx(HFULL(hs), static_cast<uint32_t>(S::HDR_Q + 2 * S::TABB));
+    bulk_load(hd, static_cast<const uint8_t*>(p.q) + (static_cast<size_t>(b) * p.Hq + h0) * S::ROWB,
+              S::HDR_Q, HFULL(hs));
+    bulk_load(hd + S::HDR_Q, cosb + trow, S::TABB, HFULL(hs));
+    bulk_load(hd + S::HDR_Q + S::TABB, sinb + trow, S::TABB, HFULL(hs));
+  };
+  // Chunk c0 of unit bk into ring stage s (producer thread). Whole boxes always land (rows past
+  // the cache or the tables are zero-filled and masked by the consumers), so every stage
+  // completes the same byte count.
+  auto issue_chunk = [&](int bk, int c0, int s) {
+    const int tpos = static_cast<int>(p.kv_pos_offset + c0);
+    const uint32_t st = sbase + s * S::STAGE;
+    mbar_expect_tx(FULL(s), static_cast<uint32_t>(S::STAGE_TX));
+#pragma unroll
+    for (int blk = 0; blk < S::NBLK; ++blk) {
+      tma_load_3d(st + S::OFF_K + blk * CK * S::SPAN, &tm_k, FULL(s), blk * (S::SPAN / 2), c0, bk);
+      tma_load_3d(st + S::OFF_V + blk * CK * S::SPAN, &tm_v, FULL(s), blk * (S::SPAN / 2), c0, bk);
+    }
+#pragma unroll
+    for (int tb = 0; tb < S::TBLK; ++tb) {
+      tma_load_2d(st + S::OFF_C + tb * CK * S::TSPAN, &tm_cos, FULL(s), tb * (S::TSPAN / 2), tpos);
+      tma_load_2d(st + S::OFF_S + tb * CK * S::TSPAN, &tm_sin, FULL(s), tb * (S::TSPAN / 2), tpos);
+    }
+  };
+  // The producer thread initialises the barriers and, unless the lengths come from a preceding
+  // kernel, issues the first item's header and first chunks before the CTA barrier, so that the
+  // first loads overlap the set-up.
+  int pre_g = 0;  // chunks issued before the barrier (all of the CTA's first item)
+  if (warp == S::NW && lane == 0) {
     for (int s = 0; s < NSTG; ++s) {
       mbar_init(FULL(s), 1);
       mbar_init(EMPTY(s), S::NW);
@@ -329,6 +368,20 @@ __global__ void __launch_bounds__(DecodeShape<D, GT>::NTHREADS, (GT == 1) ? 3 : 
     *failed = 0;
     mbar_fence_init();
     fence_proxy_async_smem();
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+    tma_prefetch_desc(&tm_cos);
+    tma_prefetch_desc(&tm_sin);
+    if (!p.varlen) {
+      DecodeWalk w0;
+      w0.init(p);
+      DecodeFrag f0;
+      if (w0.next(p, CK, f0)) {
+        issue_header(f0, 0);
+        for (int c0 = f0.kbeg; c0 < f0.kend && pre_g < NSTG; c0 += CK, ++pre_g)
+          issue_chunk(f0.unit / p.n_gchunk, c0, pre_g);
+      }
+    }
   }
   __syncthreads();
   // Per-sequence lengths: the prep kernel (this launch's programmatic predecessor) has written
@@ -338,8 +391,6 @@ __global__ void __launch_bounds__(DecodeShape<D, GT>::NTHREADS, (GT == 1) ? 3 : 
     fence_proxy_async_global();  // the appended rows are read by TMA (async proxy)
   }
 
-  const uint8_t* cosb = static_cast<const uint8_t*>(p.cos);
-  const uint8_t* sinb = static_cast<const uint8_t*>(p.sin);
 #ifdef DU_TRACE
   if (threadIdx.x == 0) trace_ev(1);
 #endif
@@ -347,10 +398,6 @@ __global__ void __launch_bounds__(DecodeShape<D, GT>::NTHREADS, (GT == 1) ? 3 : 
   if (warp == S::NW) {
     // ------------------------------------------------------------------ bulk-copy producer
     if (lane == 0) {
-      tma_prefetch_desc(&tm_k);
-      tma_prefetch_desc(&tm_v);
-      tma_prefetch_desc(&tm_cos);
-      tma_prefetch_desc(&tm_sin);
       int g = 0;  // chunk counter across items (ring stage / phase)
       bool ok = true;
       int it = 0;
@@ -358,49 +405,24 @@ __global__ void __launch_bounds__(DecodeShape<D, GT>::NTHREADS, (GT == 1) ? 3 : 
       walk.init(p);
       DecodeFrag fr;
       for (; ok && walk.next(p, CK, fr); ++it) {
-        const int unit = fr.unit;
-        const int gch = unit % p.n_gchunk;
-        const int bk = unit / p.n_gchunk;  // b * Hkv + kvh
-        const int kbeg = fr.kbeg;
-        const int kend = fr.kend;
-        {
-          // Item header: query rows of the GT heads and the cos / sin rows at q_pos.
+        const int bk = fr.unit / p.n_gchunk;  // b * Hkv + kvh
+        const bool pre = !p.varlen && it == 0;  // header and first chunks already issued
+        if (!pre) {
           const int hs = it % S::NHDR;
           if (it >= S::NHDR && !mbar_wait(HEMPTY(hs), ((it / S::NHDR) - 1) & 1, failed, 65)) {
             ok = false;
             break;
           }
-          const int b = bk / p.Hkv;
-          const int h0 = (bk - b * p.Hkv) * p.G + gch * GT;
-          const uint32_t hd = sbase + S::OFF_HDR + hs * S::HDR;
-          const size_t trow = static_cast<size_t>(fr.qpos) * S::TABB;
-          mbar_expect_tx(HFULL(hs), static_cast<uint32_t>(S::HDR_Q + 2 * S::TABB));
-          bulk_load(hd, static_cast<const uint8_t*>(p.q) + (static_cast<size_t>(b) * p.Hq + h0) * S::ROWB,
-                    S::HDR_Q, HFULL(hs));
-          bulk_load(hd + S::HDR_Q, cosb + trow, S::TABB, HFULL(hs));
-          bulk_load(hd + S::HDR_Q + S::TABB, sinb + trow, S::TABB, HFULL(hs));
+          issue_header(fr, hs);
         }
-        for (int c0 = kbeg; c0 < kend; c0 += CK, ++g) {
+        for (int c0 = fr.kbeg; c0 < fr.kend; c0 += CK, ++g) {
+          if (pre && g < pre_g) continue;
           const int s = g % NSTG;
           if (g >= NSTG && !mbar_wait(EMPTY(s), ((g / NSTG) - 1) & 1, failed, 60)) {
             ok = false;
             break;
           }
-          // Whole boxes always land (rows past the cache or the tables are zero-filled and
-          // masked by the consumers), so every stage completes the same byte count.
-          const int tpos = static_cast<int>(p.kv_pos_offset + c0);
-          const uint32_t st = sbase + s * S::STAGE;
-          mbar_expect_tx(FULL(s), static_cast<uint32_t>(S::STAGE_TX));
-#pragma unroll
-          for (int blk = 0; blk < S::NBLK; ++blk) {
-            tma_load_3d(st + S::OFF_K + blk * CK * S::SPAN, &tm_k, FULL(s), blk * (S::SPAN / 2), c0, bk);
-            tma_load_3d(st + S::OFF_V + blk * CK * S::SPAN, &tm_v, FULL(s), blk * (S::SPAN / 2), c0, bk);
-          }
-#pragma unroll
-          for (int tb = 0; tb < S::TBLK; ++tb) {
-            tma_load_2d(st + S::OFF_C + tb * CK * S::TSPAN, &tm_cos, FULL(s), tb * (S::TSPAN / 2), tpos);
-            tma_load_2d(st + S::OFF_S + tb * CK * S::TSPAN, &tm_sin, FULL(s), tb * (S::TSPAN / 2), tpos);
-          }
+          issue_chunk(bk, c0, s);
         }
       }
       // Drain: the last copies land before the CTA may exit.
