@@ -77,6 +77,11 @@ struct DecodeParams {
   void* fin_out;
   int fin_kind;
   float* fin_lse;
+  // Split walk (n_split > 1, no per-sequence lengths): chunks charged to the start of every unit
+  // when the CTAs' ranges are cut (0: equal ranges of the real chunks). A CTA whose range
+  // reaches into a second unit finishes, combines and restarts; charging that restart as
+  // frag_pen chunks gives such CTAs fewer real chunks, so they end with the others.
+  int frag_pen;
 };
 
 // Workspace of the split walk: the ticket counters first (fixed size, so that calls of any
@@ -98,9 +103,11 @@ struct DecodeFrag {
 
 // The CTA's work, walked identically by its producer and consumers. With one slot per row, whole
 // units are dealt round-robin. Otherwise the flattened (unit, chunk) sequence is cut into equal
-// contiguous ranges, one per CTA (per-CTA work differs by at most one chunk, whatever the unit
-// count), and each range into per-unit fragments; a unit's fragments go to consecutive CTAs,
-// the first of them writing slot 0.
+// contiguous ranges, one per CTA, and each range into per-unit fragments; a unit's fragments go
+// to consecutive CTAs, the first of them writing slot 0. The cut is made on a virtual sequence
+// in which unit u takes positions [u (cpu + P), (u + 1)(cpu + P)), its first P = frag_pen
+// positions standing for the cost of a fragment's start and the rest for its cpu chunks; with
+// P = 0 per-CTA work differs by at most one chunk, whatever the unit count.
 struct DecodeWalk {
   long long cur, hi;
   long long per;  // per-sequence lengths: chunks per CTA
@@ -137,15 +144,23 @@ struct DecodeWalk {
       cur = blockIdx.x;
       hi = p.n_units;
     } else {
-      cur = static_cast<long long>(blockIdx.x) * p.total_chunks / gridDim.x;
-      hi = static_cast<long long>(blockIdx.x + 1) * p.total_chunks / gridDim.x;
+      const long long vt = vtotal(p);
+      cur = static_cast<long long>(blockIdx.x) * vt / gridDim.x;
+      hi = static_cast<long long>(blockIdx.x + 1) * vt / gridDim.x;
     }
   }
-  // CTA whose range holds global chunk x.
+  // Length of the virtual sequence the split walk cuts.
+  __device__ __forceinline__ static long long vtotal(const DecodeParams& p) {
+    return static_cast<long long>(p.n_units) * (p.cpu + p.frag_pen);
+  }
+  // CTA whose range holds global chunk x (of the real sequence).
   __device__ __forceinline__ static int cta_of(const DecodeParams& p, long long x) {
     const long long G = gridDim.x;
-    long long c = x * G / p.total_chunks;
-    if ((c + 1) * p.total_chunks / G <= x) ++c;
+    const long long vt = vtotal(p);
+    const long long u = x / p.cpu;
+    const long long v = u * (p.cpu + p.frag_pen) + p.frag_pen + (x - u * p.cpu);
+    long long c = v * G / vt;
+    if ((c + 1) * vt / G <= v) ++c;
     return static_cast<int>(c);
   }
   __device__ __forceinline__ bool next(const DecodeParams& p, int CK, DecodeFrag& f) {
@@ -189,16 +204,24 @@ struct DecodeWalk {
       cur += gridDim.x;
       return true;
     }
-    const long long u = cur / p.cpu;
-    const long long ub = u * p.cpu;
-    const long long b = min(hi, ub + p.cpu);
-    f.unit = static_cast<int>(u);
-    f.kbeg = static_cast<int>(cur - ub) * CK;
-    f.kend = min(p.L, static_cast<int>(b - ub) * CK);
-    f.slot = static_cast<int>(blockIdx.x) - cta_of(p, ub);
-    f.last = (b == ub + p.cpu);
-    cur = b;
-    return true;
+    // Virtual positions [cur, hi): a range holding only a unit's start positions is skipped.
+    const long long span = p.cpu + p.frag_pen;
+    while (cur < hi) {
+      const long long u = cur / span;
+      const long long vb = u * span + p.frag_pen;  // the unit's first chunk
+      const long long e = min(hi, (u + 1) * span);
+      const long long c0 = cur > vb ? cur - vb : 0;
+      const long long c1 = e > vb ? e - vb : 0;
+      cur = e;
+      if (c1 <= c0) continue;
+      f.unit = static_cast<int>(u);
+      f.kbeg = static_cast<int>(c0) * CK;
+      f.kend = min(p.L, static_cast<int>(c1) * CK);
+      f.slot = static_cast<int>(blockIdx.x) - cta_of(p, u * p.cpu);
+      f.last = (c1 == p.cpu);
+      return true;
+    }
+    return false;
   }
 };
 

@@ -131,6 +131,7 @@ __global__ void __launch_bounds__(352, 1)
   // verdict is in the shared word fm_word (FMB).
   const uint32_t BAR_FMA = bar(S::B_FMA), BAR_FMB = bar(S::B_FMB);
   volatile int* fm_word = reinterpret_cast<volatile int*>(sgen + S::OFF_MISC + 8);
+  int done_t = -1;  // thread 0: this CTA's ticket on the finished-CTA counter (-1: not taken)
   const uint32_t tmem_slot = sbase + S::OFF_MISC;
   volatile int* failed = reinterpret_cast<volatile int*>(sgen + S::OFF_MISC + 4);
   float* mrg = reinterpret_cast<float*>(sgen + S::OFF_MRG);  // o [4][GT][D], m [4][GT], l [4][GT]
@@ -589,15 +590,18 @@ __global__ void __launch_bounds__(352, 1)
       ok = __all_sync(0xffffffffu, mbar_wait(OD((g - 1) & 1), ((g - 1) >> 1) & 1, failed, 726));
       if (!ok) break;
       tc_fence_after();
+      // O in batches of four 16-column loads per wait.
+      constexpr int OB = (D >= 64) ? 64 : D;
 #pragma unroll 1
-      for (int c = 0; c < D; c += 16) {
-        float o[16];
-        tmem_ld16(tmem + lane_off + S::TM_O + c, o);
+      for (int c0 = 0; c0 < D; c0 += OB) {
+        float o[OB];
+#pragma unroll
+        for (int c = 0; c < OB; c += 16) tmem_ld16(tmem + lane_off + S::TM_O + c0 + c, o + c);
         tmem_wait_ld();
         if (lane < GT) {
-          float4* dst = reinterpret_cast<float4*>(mrg + (warp * GT + lane) * D + c);
+          float4* dst = reinterpret_cast<float4*>(mrg + (warp * GT + lane) * D + c0);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+          for (int i = 0; i < OB / 4; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
         }
       }
       if (lane < GT) {
@@ -645,6 +649,12 @@ __global__ void __launch_bounds__(352, 1)
             const int nf = DecodeWalk::cta_of(p, ub + p.cpu - 1) - DecodeWalk::cta_of(p, ub) + 1;
             verdict = (atomicAdd(&p.unit_cnt[fr.unit], 1) == nf - 1) ? nf : 0;
             if (verdict > 0) __threadfence();
+            // After the CTA's last unit ticket, its ticket on the finished-CTA counter: the
+            // counters may be zeroed once every CTA has taken its unit tickets, so this one is
+            // taken now and its value read only at the end (the round trip overlaps the merge).
+            DecodeWalk peek = walk;
+            DecodeFrag nx;
+            if (!peek.next(p, CK, nx)) done_t = atomicAdd(&p.unit_cnt[DECODE_CNT_DONE], 1);
           }
           *fm_word = verdict;
           mbar_arrive(BAR_FMB);
@@ -721,12 +731,13 @@ __global__ void __launch_bounds__(352, 1)
   if (tid == 0) trace_ev(5);
 #endif
   if (p.fused_merge && !p.varlen) {
-    // The last CTA to finish zeroes the tickets for the next call (every CTA gets here, also
-    // after a failed wait, so the counters never stay dirty).
+    // The last CTA to take its finished-CTA ticket zeroes the counters for the next call (every
+    // CTA gets here, also after a failed wait, so the counters never stay dirty). A CTA takes
+    // that ticket only after all of its unit tickets, so none is taken after the zeroing.
     __syncthreads();
     if (tid == 0) {
-      __threadfence();
-      *fm_word = (atomicAdd(&p.unit_cnt[DECODE_CNT_DONE], 1) == static_cast<int>(gridDim.x) - 1) ? 1 : 0;
+      if (done_t < 0) done_t = atomicAdd(&p.unit_cnt[DECODE_CNT_DONE], 1);
+      *fm_word = (done_t == static_cast<int>(gridDim.x) - 1) ? 1 : 0;
     }
     __syncthreads();
     if (*fm_word == 1) {

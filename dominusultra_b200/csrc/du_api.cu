@@ -365,6 +365,7 @@ struct DecodePlan {
   int cpu;       // chunks per unit
   long long total_chunks;
   int grid;      // CTAs launched (the kernel's resident count per SM x SMs, or fewer)
+  int frag_pen;  // chunks charged to each unit start when the split walk cuts CTA ranges
 };
 
 // Keys per ring stage of the decode kernel instantiated for (D, GT): splits are whole chunks.
@@ -463,7 +464,17 @@ DecodePlan plan_decode(int B, int Hq, int Hkv, int L, int D) {
     pl.n_split = static_cast<int>(k);  // k == 1: whole units, final rows written directly
     return pl;
   }
-  long long slots = (pl.cpu - 1 + per - 1) / per + 1;  // CTAs one unit's chunks can span
+  // Spread over every CTA. On the tensor-core kernel a CTA's second fragment costs a few
+  // chunks' time (combine, ticket, merge, restart; a per-CTA timeline of B4 H32 Hkv8 D128
+  // L16384 showed the two-fragment CTAs ending ~5 us after the others), so each unit start is
+  // charged that many chunks when the ranges are cut (DecodeWalk) and such CTAs take fewer.
+  // Measured (graph-timed, B200) charging 0 / 4 / 6 chunks: L16384 63.9 / 60.6 / 60.8 us,
+  // eight-head units (H64) L16384 76.6 / 71.5 / 70.0, L20000 74.0 / 70.3 / 71.4, L65536
+  // 196.8 / 194.2 / 193.6.
+  pl.frag_pen = decode_use_tc(D, pl.GT) ? (pl.GT == 8 ? 6 : 4) : 0;
+  // A CTA inside one unit holds at least vper of its chunks, so a unit spans at most this many.
+  const long long vper = units * (pl.cpu + pl.frag_pen) / grid;
+  long long slots = (pl.cpu - 1 + vper - 1) / vper + 1;
   if (slots < 2) slots = 2;
   pl.grid = static_cast<int>(grid);
   pl.n_split = static_cast<int>(slots);
@@ -635,6 +646,7 @@ int decode_impl(const void* q, const void* kc, const void* vc, const void* cos, 
   prm.n_units = pl.n_units;
   prm.cpu = pl.cpu;
   prm.total_chunks = pl.total_chunks;
+  prm.frag_pen = pl.frag_pen;
   prm.q_pos = q_pos;
   prm.kv_pos_offset = kv_off;
   prm.scale_log2 = scale * 1.4426950408889634f;
