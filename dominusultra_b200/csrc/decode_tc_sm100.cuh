@@ -638,17 +638,15 @@ __global__ void __launch_bounds__(352, 1)
       if (p.fused_merge && !p.varlen && fr.slot >= 0) {
         // Ticket: the fragment that completes the unit merges its GT rows. The consumer threads'
         // partial stores reach thread 0 through the barrier (release / acquire in the CTA); its
-        // fence makes them visible device-wide before the ticket, and after the last ticket
-        // makes the other fragments' partials visible to this CTA.
+        // ticket is an acquire-release add, which makes them visible device-wide before the
+        // ticket and, after the last ticket, the other fragments' partials visible to this CTA.
         mbar_arrive(BAR_FMA);
         if (tid == 0) {
           int verdict = -1;
           if (mbar_wait(BAR_FMA, fmq & 1, failed, 729)) {
-            __threadfence();
             const long long ub = static_cast<long long>(fr.unit) * p.cpu;
             const int nf = DecodeWalk::cta_of(p, ub + p.cpu - 1) - DecodeWalk::cta_of(p, ub) + 1;
-            verdict = (atomicAdd(&p.unit_cnt[fr.unit], 1) == nf - 1) ? nf : 0;
-            if (verdict > 0) __threadfence();
+            verdict = (atom_add_acq_rel_gpu(&p.unit_cnt[fr.unit], 1) == nf - 1) ? nf : 0;
             // After the CTA's last unit ticket, its ticket on the finished-CTA counter: the
             // counters may be zeroed once every CTA has taken its unit tickets, so this one is
             // taken now and its value read only at the end (the round trip overlaps the merge).

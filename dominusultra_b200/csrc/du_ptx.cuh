@@ -200,6 +200,15 @@ __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity, u
   return true;
 }
 
+// Device-scope atomic add with acquire-release semantics: this thread's earlier writes, and those
+// of threads it has synchronised with, are visible device-wide before the add; writes released
+// by earlier adds on the same word are visible to this thread after it.
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* addr, int v) {
+  int old;
+  asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], %2;" : "=r"(old) : "l"(addr), "r"(v) : "memory");
+  return old;
+}
+
 // ---------------------------------------------------------------------------------------------
 // proxy fences
 // ---------------------------------------------------------------------------------------------

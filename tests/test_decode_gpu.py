@@ -172,6 +172,8 @@ TC_CASES = [
     (2, 16, 2, 3000, torch.bfloat16),    # group 8: eight-head units
     (1, 64, 4, 5000, torch.float16),     # group 16: two eight-head units per KV head
     (24, 64, 8, 300, torch.bfloat16),    # 192 eight-head units
+    (25, 16, 4, 2048, torch.bfloat16),   # 100 units of 16 chunks: many CTAs reach into a second unit
+    (7, 32, 8, 5000, torch.float16),     # ragged last chunk, CTAs cut with unit starts charged
 ]
 
 
@@ -202,7 +204,8 @@ def test_decode_four_head_partial_outputs(cuda_device):
 
 
 @pytest.mark.parametrize("B,Hq,Hkv,L,D", [(4, 32, 8, 16384, 128), (1, 64, 8, 20000, 128),
-                                          (2, 32, 8, 3000, 128)])
+                                          (2, 32, 8, 3000, 128), (25, 16, 4, 2048, 128),
+                                          (4, 64, 8, 16384, 128)])
 def test_decode_split_merge_in_kernel_leaves_counters_zero(cuda_device, B, Hq, Hkv, L, D):
     """The tensor-core decode merges a unit's partials inside the split kernel: the CTA that
     takes the unit's last ticket merges. Two calls in a row on one zero-filled workspace match
