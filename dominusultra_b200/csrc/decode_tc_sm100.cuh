@@ -62,13 +62,13 @@ struct DecodeTcShape {
   static constexpr int MRG_BYTES = 4 * GT * D * 4 + 2 * 4 * GT * 4;
   static constexpr int OFF_BAR = OFF_MRG + MRG_BYTES;
   // full, empty, vfull, vempty, rk: one per stage; then sf, sc, od[2], pf[2], qr, mrg,
-  // hfull[2], hempty[2], drain
+  // hfull[2], hempty[2], drain, fma, fmb, k0 (the CTA's first K chunk has landed; one phase)
   static constexpr int B_FULL = 0, B_EMPTY = NSTG, B_VFULL = 2 * NSTG, B_VEMPTY = 3 * NSTG,
                        B_RK = 4 * NSTG, B_SF = 5 * NSTG, B_SC = B_SF + 1, B_OD = B_SF + 2,
                        B_PF = B_SF + 4, B_QR = B_SF + 6, B_MRG = B_SF + 7, B_HFULL = B_SF + 8,
                        B_HEMPTY = B_SF + 10, B_DR = B_SF + 12, B_FMA = B_SF + 13,
-                       B_FMB = B_SF + 14;
-  static constexpr int N_BAR = B_FMB + 1;
+                       B_FMB = B_SF + 14, B_K0 = B_SF + 15;
+  static constexpr int N_BAR = B_K0 + 1;
   static constexpr int OFF_MISC = OFF_BAR + 8 * N_BAR;     // tmem address, failure flag
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
   static constexpr int TMEM_COLS = 512;
@@ -130,6 +130,7 @@ __global__ void __launch_bounds__(352, 1)
   // Fused merge: every consumer thread's partial is stored and fenced (FMA); the ticket's
   // verdict is in the shared word fm_word (FMB).
   const uint32_t BAR_FMA = bar(S::B_FMA), BAR_FMB = bar(S::B_FMB);
+  const uint32_t BAR_K0 = bar(S::B_K0);
   volatile int* fm_word = reinterpret_cast<volatile int*>(sgen + S::OFF_MISC + 8);
   int done_t = -1;  // thread 0: this CTA's ticket on the finished-CTA counter (-1: not taken)
   const uint32_t tmem_slot = sbase + S::OFF_MISC;
@@ -176,6 +177,7 @@ __global__ void __launch_bounds__(352, 1)
     mbar_init(BAR_DR, 1);
     mbar_init(BAR_FMA, 128);
     mbar_init(BAR_FMB, 1);
+    mbar_init(BAR_K0, 1);
     *failed = 0;
     mbar_fence_init();
     fence_proxy_async_smem();
@@ -290,6 +292,14 @@ __global__ void __launch_bounds__(352, 1)
             ok = false;
             break;
           }
+          // The CTA's first V waits until its first K chunk (with the tables) has landed: at the
+          // start every CTA's whole ring is requested at once and the first chunk, needed first,
+          // shares the bandwidth with the rest (B4 H32 Hkv8 D128 L16384 59.3 -> 58.7 us). The
+          // rotation group signals that landing on a barrier with a single phase.
+          if (g == 0 && !mbar_wait(BAR_K0, 0, failed, 707)) {
+            ok = false;
+            break;
+          }
           const uint32_t st = sbase + S::OFF_VR + s * S::KV_BYTES;
           mbar_expect_tx(VFULL(s), static_cast<uint32_t>(S::KV_BYTES));
 #pragma unroll
@@ -378,6 +388,7 @@ __global__ void __launch_bounds__(352, 1)
     auto rotate_chunk = [&](int gg) -> bool {
       const int s = gg % S::NSTG;
       if (!__all_sync(0xffffffffu, mbar_wait(FULL(s), (gg / S::NSTG) & 1, failed, 720))) return false;
+      if (gg == 0 && tid == 224) mbar_arrive(BAR_K0);
 #ifdef DU_TRACE
       if (tid == 224 && gg == 0) trace_ev(7);
 #endif
