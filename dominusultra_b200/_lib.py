@@ -69,6 +69,15 @@ SIGNATURES = {
         _i,
         [_vp, _vp, _i, _i, _i, _ll, _ll, _ll, _ll, _vp, _i, _vp, _vp],
     ),
+    "du_exchange_buffer_bytes": (_sz, [_i, _i, _i]),
+    "du_exchange_buffer_alloc": (_i, [_sz, ctypes.POINTER(_vp)]),
+    "du_exchange_buffer_free": (_i, [_vp]),
+    "du_ipc_get_handle": (_i, [_vp, _vp]),
+    "du_ipc_open_handle": (_i, [_vp, ctypes.POINTER(_vp)]),
+    "du_ipc_close_handle": (_i, [_vp]),
+    "du_exchange_merge": (
+        _i, [_vp, _vp, ctypes.POINTER(_vp), _i, _i, _i, _i, _vp, _i, _vp, _vp]
+    ),
     "du_decode_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _ll, _vp]),
     "du_selftest_wait_timeout": (_i, [_i, _vp]),
     "du_read_status": (_i, [ctypes.POINTER(ctypes.c_uint), _i]),

@@ -18,6 +18,7 @@
 #include "../../include/dominus_ultra_b200.h"
 #include "decode_sm100.cuh"
 #include "decode_tc_sm100.cuh"
+#include "exchange_sm100.cuh"
 #include "prefill_fa1_sm100.cuh"
 #include "prefill_fa_sm100.cuh"
 #include "prefill_sm100.cuh"
@@ -1076,6 +1077,103 @@ int du_merge_partials(const float* o_parts, const float* lse_parts, int R, int r
     return fail(DU_ERR_INVALID, "out_dtype must be DU_DTYPE_F16, BF16 or F32");
   return launch_merge(o_parts, lse_parts, R, rows, D, o_stride_r, o_stride_row, lse_stride_r,
                       lse_stride_row, out, out_dtype, lse_out, static_cast<cudaStream_t>(stream));
+}
+
+
+// --------------------------------------------------------------------------------------------
+// Peer-memory exchange of sequence-split decode partials (exchange_sm100.cuh)
+// --------------------------------------------------------------------------------------------
+size_t du_exchange_buffer_bytes(int world, int rows, int D) {
+  if (world < 1 || world > du::XCH_MAX_WORLD || rows <= 0 || D <= 0 || D % 4 != 0) return 0;
+  return du::XchLayout::bytes(world, rows, D);
+}
+
+int du_exchange_buffer_alloc(size_t bytes, void** ptr) {
+  g_last_error.clear();
+  if (ptr == nullptr || bytes == 0) return fail(DU_ERR_INVALID, "null pointer or zero size");
+  *ptr = nullptr;
+  // Its own allocation, so that a CUDA IPC handle covers exactly this buffer.
+  cudaError_t e = cudaMalloc(ptr, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(exchange buffer)");
+  e = cudaMemset(*ptr, 0, bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    cudaFree(*ptr);
+    *ptr = nullptr;
+    return cuda_fail(e, "cudaMemset(exchange buffer)");
+  }
+  return DU_OK;
+}
+
+int du_exchange_buffer_free(void* ptr) {
+  g_last_error.clear();
+  if (ptr == nullptr) return DU_OK;
+  cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? DU_OK : cuda_fail(e, "cudaFree(exchange buffer)");
+}
+
+int du_ipc_get_handle(const void* ptr, void* handle64) {
+  g_last_error.clear();
+  if (ptr == nullptr || handle64 == nullptr) return fail(DU_ERR_INVALID, "null pointer argument");
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "CUDA IPC handles are 64 bytes");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(ptr));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+  std::memcpy(handle64, &h, sizeof(h));
+  return DU_OK;
+}
+
+int du_ipc_open_handle(const void* handle64, void** ptr) {
+  g_last_error.clear();
+  if (ptr == nullptr || handle64 == nullptr) return fail(DU_ERR_INVALID, "null pointer argument");
+  *ptr = nullptr;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle64, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  return e == cudaSuccess ? DU_OK : cuda_fail(e, "cudaIpcOpenMemHandle");
+}
+
+int du_ipc_close_handle(void* ptr) {
+  g_last_error.clear();
+  if (ptr == nullptr) return DU_OK;
+  cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  return e == cudaSuccess ? DU_OK : cuda_fail(e, "cudaIpcCloseMemHandle");
+}
+
+int du_exchange_merge(const float* o_local, const float* lse_local, void* const* buffers, int world,
+                      int rank, int rows, int D, void* out, int out_dtype, float* lse_out,
+                      void* stream) {
+  g_last_error.clear();
+  if (world < 1 || world > du::XCH_MAX_WORLD)
+    return fail(DU_ERR_UNSUPPORTED, "world must be between 1 and " + std::to_string(du::XCH_MAX_WORLD));
+  if (rank < 0 || rank >= world) return fail(DU_ERR_INVALID, "rank must be in [0, world)");
+  if (rows <= 0 || D <= 0 || D % 4 != 0) return fail(DU_ERR_INVALID, "rows must be positive and D a multiple of 4");
+  if (!o_local || !lse_local || !buffers || !out) return fail(DU_ERR_INVALID, "null pointer argument");
+  if (!aligned16(o_local)) return fail(DU_ERR_INVALID, "o_local must be 16-byte aligned");
+  if (out_dtype != DU_DTYPE_F16 && out_dtype != DU_DTYPE_BF16 && out_dtype != DU_DTYPE_F32)
+    return fail(DU_ERR_INVALID, "out_dtype must be DU_DTYPE_F16, BF16 or F32");
+  du::XchParams p{};
+  for (int r = 0; r < world; ++r) {
+    if (buffers[r] == nullptr || reinterpret_cast<uintptr_t>(buffers[r]) % 256 != 0)
+      return fail(DU_ERR_INVALID, "every exchange buffer must be non-null and 256-byte aligned");
+    p.peer[r] = static_cast<uint8_t*>(buffers[r]);
+  }
+  p.o_loc = o_local;
+  p.lse_loc = lse_local;
+  p.world = world;
+  p.rank = rank;
+  p.rows = rows;
+  p.D = D;
+  const int grid0 = rows < du::XCH_MAX_CTAS ? rows : du::XCH_MAX_CTAS;
+  p.rpc = (rows + grid0 - 1) / grid0;
+  const int grid = (rows + p.rpc - 1) / p.rpc;
+  p.o_bytes = du::XchLayout::o_bytes(world, rows, D);
+  p.out = out;
+  p.out_kind = out_dtype == DU_DTYPE_F32 ? 2 : (out_dtype == DU_DTYPE_BF16 ? 1 : 0);
+  p.lse_out = lse_out;
+  du::xch_merge_kernel<<<grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? DU_OK : cuda_fail(e, "exchange merge launch");
 }
 
 }  // extern "C"

@@ -13,6 +13,10 @@ The reference has no multi-GPU code; this module follows the partitioning the pa
   ``all_gather_into_tensor`` (NCCL over NVLink), and each rank merges them by LSE
   (``merge_partials``). This is the only collective on the path.
 
+  ``PeerExchange`` replaces that collective and the merge launch with one kernel over NVLink
+  peer memory (``du_exchange_merge``): each rank stores its partial into every rank's exchange
+  buffer (mapped once through CUDA IPC) and merges the world's partials as soon as they are in.
+
 The compute functions are injectable so the host logic (unit ranges, packing, collective,
 merge) is testable on CPU ranks with the gloo backend and the oracle.
 """
@@ -131,6 +135,97 @@ def unpack_gathered(gathered: torch.Tensor, world: int, rows_shape, D: int):
     return o, lse
 
 
+class PeerExchange:
+    """Exchange buffers of the sequence-split decode, mapped on every rank of ``group`` (one
+    node, one GPU per rank, at most 8 ranks) for ``rows`` partial rows of ``D`` values.
+
+    Set-up is collective (every rank constructs it, in the same order as its other collectives):
+    each rank allocates its buffer (``du_exchange_buffer_alloc``), the 64-byte CUDA IPC handles
+    travel with ``all_gather_object``, and each rank opens the others'. ``merge`` then runs
+    ``du_exchange_merge`` on the current stream. ``close`` (also collective) unmaps and frees.
+    """
+
+    def __init__(self, rows: int, D: int, group=None, device=None):
+        import ctypes
+
+        import torch.distributed as dist
+
+        from . import _lib
+
+        self._lib = _lib.load()
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.rows, self.D = rows, D
+        self.device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        nbytes = int(self._lib.du_exchange_buffer_bytes(self.world, rows, D))
+        if nbytes == 0:
+            raise ValueError("peer exchange supports 1..8 ranks and D a multiple of 4")
+        with torch.cuda.device(self.device):
+            own = ctypes.c_void_p()
+            _lib.check(self._lib.du_exchange_buffer_alloc(nbytes, ctypes.byref(own)), "du_exchange_buffer_alloc")
+            handle = ctypes.create_string_buffer(64)
+            _lib.check(self._lib.du_ipc_get_handle(own, handle), "du_ipc_get_handle")
+            handles: list = [None] * self.world
+            dist.all_gather_object(handles, handle.raw, group=group)
+            ptrs = []
+            self._opened = []
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    ptrs.append(own.value)
+                    continue
+                peer = ctypes.c_void_p()
+                _lib.check(self._lib.du_ipc_open_handle(ctypes.create_string_buffer(h, 64), ctypes.byref(peer)),
+                           "du_ipc_open_handle")
+                self._opened.append(peer.value)
+                ptrs.append(peer.value)
+        self._own = own.value
+        self._ptrs = (ctypes.c_void_p * self.world)(*ptrs)
+
+    def merge(self, o_local: torch.Tensor, lse_local: torch.Tensor, out_dtype: torch.dtype,
+              with_lse: bool = False):
+        """Merge every rank's ``(o [*rows, D], lse [*rows])`` fp32 partial; returns ``out`` in
+        ``out_dtype`` (and the merged lse with ``with_lse``) on every rank."""
+        import ctypes
+
+        from . import _lib
+        from .attention import _dtype_code
+
+        if o_local.dtype != torch.float32 or lse_local.dtype != torch.float32:
+            raise ValueError("partials must be float32")
+        o2 = o_local.reshape(-1, self.D)
+        l2 = lse_local.reshape(-1)
+        if o2.shape[0] != self.rows or l2.shape[0] != self.rows or not (o2.is_contiguous() and l2.is_contiguous()):
+            raise ValueError("partials must be contiguous [rows, D] / [rows] blocks of this exchange's rows")
+        out = torch.empty(o_local.shape, dtype=out_dtype, device=o_local.device)
+        lse = torch.empty(lse_local.shape, dtype=torch.float32, device=o_local.device) if with_lse else None
+        st = ctypes.c_void_p(torch.cuda.current_stream(o_local.device).cuda_stream)
+        rc = self._lib.du_exchange_merge(
+            ctypes.c_void_p(o2.data_ptr()), ctypes.c_void_p(l2.data_ptr()), self._ptrs, self.world,
+            self.rank, self.rows, self.D, ctypes.c_void_p(out.data_ptr()), _dtype_code(out_dtype),
+            ctypes.c_void_p(lse.data_ptr()) if lse is not None else None, st)
+        _lib.check(rc, "du_exchange_merge")
+        return out, lse
+
+    def close(self):
+        """Collective: unmap the peers' buffers and free this rank's (after a barrier, so no
+        rank frees a buffer another may still write)."""
+        import torch.distributed as dist
+
+        from . import _lib
+
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for p in self._opened:
+            _lib.check(self._lib.du_ipc_close_handle(p), "du_ipc_close_handle")
+        self._opened = []
+        dist.barrier(group=self.group)
+        _lib.check(self._lib.du_exchange_buffer_free(self._own), "du_exchange_buffer_free")
+        self._own = None
+
+
 def sharded_decode(
     q_new: torch.Tensor,
     k_shard: torch.Tensor,
@@ -143,6 +238,7 @@ def sharded_decode(
     group=None,
     partial_fn: Optional[Callable] = None,
     merge_fn: Optional[Callable] = None,
+    exchange: Optional[PeerExchange] = None,
 ) -> torch.Tensor:
     """Decode over a KV sequence split across the ranks of ``group``.
 
@@ -159,6 +255,9 @@ def sharded_decode(
     world = dist.get_world_size(group)
     B, Hq, _, D = q_new.shape
     o, lse = partial_fn(q_new, k_shard, v_shard, cos, sin, num_kv_heads, total_len, kv_pos_offset)
+    if exchange is not None:
+        out, _ = exchange.merge(o, lse, q_new.dtype)
+        return out.reshape(B, Hq, 1, D)
     send = pack_partial(o, lse)
     gathered = torch.empty(world * send.numel(), dtype=send.dtype, device=send.device)
     dist.all_gather_into_tensor(gathered, send, group=group)

@@ -182,6 +182,32 @@ int du_merge_partials(const float* o_parts, const float* lse_parts, int R, int r
                       void* stream);
 
 /*
+ * Collective + merge step of the sequence-split decode over NVLink peer memory (no counterpart
+ * in the reference, which runs on one GPU; it replaces the NCCL all-gather of the packed
+ * partials followed by du_merge_partials). Every rank of one node owns an exchange buffer of
+ * du_exchange_buffer_bytes(world, rows, D) bytes from du_exchange_buffer_alloc (zero-filled, its
+ * own cudaMalloc allocation so that a CUDA IPC handle covers it), publishes its handle
+ * (du_ipc_get_handle, 64 bytes) and opens the others' (du_ipc_open_handle). du_exchange_merge
+ * then takes this rank's fp32 partial (o_local [rows, D], lse_local [rows], e.g. from
+ * du_decode_partial), stores it into slot `rank` of every rank's buffer, waits (bounded) for the
+ * other ranks' slots, and writes the LSE merge of all `world` partials into out [rows, D]
+ * (out_dtype) and, when non-NULL, lse_out [rows] (natural log). buffers[r] is rank r's buffer as
+ * this process maps it (its own allocation for r == rank). Every rank must make the same calls,
+ * in the same order, with the same world, rows and D; a rank may run at most one call ahead of
+ * another. A wait that expires is reported by du_read_status (code 5, sites 900 + rank) and
+ * leaves that block's rows unwritten. world <= 8, D a multiple of 4.
+ */
+size_t du_exchange_buffer_bytes(int world, int rows, int D);
+int du_exchange_buffer_alloc(size_t bytes, void** ptr);
+int du_exchange_buffer_free(void* ptr);
+int du_ipc_get_handle(const void* ptr, void* handle64);
+int du_ipc_open_handle(const void* handle64, void** ptr);
+int du_ipc_close_handle(void* ptr);
+int du_exchange_merge(const float* o_local, const float* lse_local, void* const* buffers, int world,
+                      int rank, int rows, int D, void* out, int out_dtype, float* lse_out,
+                      void* stream);
+
+/*
  * Decode that allocates nothing. No counterpart in the reference: it exists for callers that
  * cannot allocate device memory themselves -- hosts that bind this C ABI from another runtime
  * without a CUDA allocator, and serving loops that must not call cudaMalloc once they are

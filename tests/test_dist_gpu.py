@@ -22,7 +22,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, q_out):
+def _worker(rank, world, port, q_out, peer=False):
     import datetime
 
     import torch.distributed as dist
@@ -47,13 +47,25 @@ def _worker(rank, world, port, q_out):
         cos, sin = precompute_rope_cos_sin(L + 1, D, "cpu", torch.bfloat16, 500000.0)
         a, b = ddist.kv_shard(L, world, rank)
         dev = torch.device("cuda", rank)
-        out = ddist.sharded_decode(q.to(dev), k[:, :, a:b].contiguous().to(dev),
-                                   v[:, :, a:b].contiguous().to(dev), cos.to(dev), sin.to(dev),
-                                   Hkv, L, a)
-        torch.cuda.synchronize()
+        ex = ddist.PeerExchange(B * Hq, D, device=dev) if peer else None
         ref = oracle.decode(q, k, v, cos, sin, Hkv)
-        err = (out.float().cpu() - ref).abs().max().item()
-        q_out.put((rank, err))
+        errs = []
+        # Two calls in a row (the peer exchange alternates its slots and flags between calls),
+        # the second on rescaled values so a stale slot would show.
+        for call in range(2 if peer else 1):
+            qs = q if call == 0 else (q * 0.5).to(torch.bfloat16)
+            out = ddist.sharded_decode(qs.to(dev), k[:, :, a:b].contiguous().to(dev),
+                                       v[:, :, a:b].contiguous().to(dev), cos.to(dev), sin.to(dev),
+                                       Hkv, L, a, exchange=ex)
+            torch.cuda.synchronize()
+            r = ref if call == 0 else oracle.decode(qs, k, v, cos, sin, Hkv)
+            errs.append((out.float().cpu() - r).abs().max().item())
+        if ex is not None:
+            from dominusultra_b200 import _lib
+            status = _lib.read_status(reset=True)
+            ex.close()
+            assert status[0] == 0, status
+        q_out.put((rank, max(errs)))
     finally:
         dist.destroy_process_group()
 
@@ -65,6 +77,26 @@ def test_sharded_decode_two_gpus_nccl():
     q = ctx.Queue()
     port = _free_port()
     procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, err in res:
+        assert err <= 2e-2, (rank, err)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_sharded_decode_two_gpus_peer_exchange():
+    """The same sequence-split decode with the partials exchanged and merged over NVLink peer
+    memory (PeerExchange, du_exchange_merge) instead of NCCL: two calls in a row on each rank
+    match the unsharded oracle, and no bounded wait expires."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, True)) for r in range(world)]
     for p in procs:
         p.start()
     res = sorted(q.get(timeout=300) for _ in range(world))
