@@ -413,7 +413,7 @@ def bench_decode_long(dist, rank, world, device, stream, steps, warmup, peaks):
     o_view = send[: rows * D].view(B, H, D)
     l_view = send[rows * D:].view(B, H)
 
-    def step(_i):
+    def step_nccl(_i):
         decode_partial(q, k, v, cos, sin, Hkv, q_pos=L, kv_pos_offset=a, out=o_view, lse=l_view)
         if dist is not None:
             dist.all_gather_into_tensor(gathered, send)
@@ -422,27 +422,64 @@ def bench_decode_long(dist, rank, world, device, stream, steps, warmup, peaks):
             o_all, l_all = o_view.unsqueeze(0), l_view.unsqueeze(0)
         merge_partials(o_all, l_all, torch.bfloat16)
 
+    # With several ranks the partials are exchanged and merged over NVLink peer memory in one
+    # kernel (PeerExchange); the NCCL all-gather + merge form is timed beside it. Every rank
+    # takes the same path: if any rank cannot map the others' buffers, all use NCCL.
+    ex = None
+    if dist is not None and world > 1:
+        try:
+            ex = ddist.PeerExchange(rows, D, device=device)
+            ok = 1
+        except RuntimeError:
+            ok = 0
+        flag = torch.tensor([ok], device=device)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        if int(flag.item()) == 0:
+            if ex is not None:
+                ex.close()  # collective: two barriers, matched below on the ranks that failed
+            else:
+                dist.barrier()
+                dist.barrier()
+            ex = None
+
+    def step_peer(_i):
+        decode_partial(q, k, v, cos, sin, Hkv, q_pos=L, kv_pos_offset=a, out=o_view, lse=l_view)
+        ex.merge(o_view, l_view, torch.bfloat16)
+
+    step = step_peer if ex is not None else step_nccl
     for i in range(warmup):
         step(i)
     torch.cuda.synchronize()
     barrier(dist)
-    # Eagerly launched, the host path of a step (three Python wrappers and the collective, ~75 us)
-    # exceeds the device time of a rank's shard at eight GPUs; a generation loop replays the step
-    # as a CUDA graph, and so does the timed region here (the eager figure is reported beside it).
+    # Eagerly launched, the host path of a step (Python wrappers and the collective, ~75 us with
+    # NCCL) exceeds the device time of a rank's shard at eight GPUs; a generation loop replays the
+    # step as a CUDA graph, and so does the timed region here (the eager figure is reported too).
     eager_ms = max_over_ranks(dist, time_region(step, steps, stream) / steps, device)
     barrier(dist)
     side = torch.cuda.Stream(device)
     ms = max_over_ranks(dist, graph_time(step, steps, side) / steps, device)
+    nccl_ms = None
+    if ex is not None:
+        for i in range(warmup):
+            step_nccl(i)
+        torch.cuda.synchronize()
+        barrier(dist)
+        nccl_ms = max_over_ranks(dist, graph_time(step_nccl, steps, side) / steps, device)
+        barrier(dist)
+        ex.close()
+    exchange = ("partials exchanged and merged over NVLink peer memory in one kernel "
+                "(du_exchange_merge)") if ex is not None else "one NCCL all-gather + merge per step"
     total_bytes = decode_bytes(B, H, Hkv, L, D)
     return {
         "metric": "long-context decode KV-cache GB/s (whole job)",
         "value": total_bytes / (ms / 1000.0) / 1e9, "unit": "GB/s", "ms_per_step": ms,
-        "timing": "CUDA graph of the steps (partial kernel, all-gather, merge), replayed between "
+        "timing": "CUDA graph of the steps (partial kernel, exchange, merge), replayed between "
                   "events; max over ranks",
         "eager_ms_per_step": eager_ms,
+        "nccl_allgather_ms_per_step": nccl_ms,
         "scaling": "strong",
         "config": {"workload": f"decode B{B} H{H} Hkv{Hkv} L{L} D{D} bf16 RoPE base 5e5, "
-                               f"KV sequence split over {world} GPU(s), one NCCL all-gather per step",
+                               f"KV sequence split over {world} GPU(s), {exchange}",
                    "kv_bytes_per_gpu": total_bytes / world},
         "per_gpu_hbm_frac": (total_bytes / world) / (ms / 1000.0) / 1e9 / peaks["hbm_gbs"],
     }
