@@ -1167,7 +1167,6 @@ int du_exchange_merge(const float* o_local, const float* lse_local, void* const*
   const int grid0 = rows < du::XCH_MAX_CTAS ? rows : du::XCH_MAX_CTAS;
   p.rpc = (rows + grid0 - 1) / grid0;
   const int grid = (rows + p.rpc - 1) / p.rpc;
-  p.o_bytes = du::XchLayout::o_bytes(world, rows, D);
   p.out = out;
   p.out_kind = out_dtype == DU_DTYPE_F32 ? 2 : (out_dtype == DU_DTYPE_BF16 ? 1 : 0);
   p.lse_out = lse_out;
