@@ -178,6 +178,29 @@ def test_c_abi_rejects_bad_arguments_before_launch():
     assert rc == _lib.DU_ERR_WORKSPACE and str(need) in _lib.last_error()
 
 
+def test_exchange_merge_rejects_bad_arguments_before_launch():
+    """The peer-memory exchange validates world, rank, sizes and its buffers before any CUDA
+    call (the kernel itself needs every rank of the call; it runs in the 2-GPU tests)."""
+    lib = _lib.load()
+    null = ctypes.c_void_p(0)
+    fake = ctypes.c_void_p(0x10000)
+    bufs = (ctypes.c_void_p * 2)(0x20000, 0x30000)
+    assert lib.du_exchange_buffer_bytes(9, 128, 128) == 0
+    assert lib.du_exchange_buffer_bytes(2, 128, 6) == 0
+    assert lib.du_exchange_buffer_bytes(2, 128, 128) == 256 + 2 * 2 * 128 * 129 * 8
+    rc = lib.du_exchange_merge(fake, fake, bufs, 9, 0, 128, 128, fake, _lib.DU_DTYPE_BF16, null, null)
+    assert rc == _lib.DU_ERR_UNSUPPORTED
+    rc = lib.du_exchange_merge(fake, fake, bufs, 2, 2, 128, 128, fake, _lib.DU_DTYPE_BF16, null, null)
+    assert rc == _lib.DU_ERR_INVALID and "rank" in _lib.last_error()
+    rc = lib.du_exchange_merge(fake, fake, bufs, 2, 0, 128, 130, fake, _lib.DU_DTYPE_BF16, null, null)
+    assert rc == _lib.DU_ERR_INVALID
+    bad = (ctypes.c_void_p * 2)(0x20000, 0x30010)  # not 256-byte aligned
+    rc = lib.du_exchange_merge(fake, fake, bad, 2, 0, 128, 128, fake, _lib.DU_DTYPE_BF16, null, null)
+    assert rc == _lib.DU_ERR_INVALID and "aligned" in _lib.last_error()
+    rc = lib.du_exchange_merge(fake, fake, bufs, 2, 0, 128, 128, fake, 7, null, null)
+    assert rc == _lib.DU_ERR_INVALID and "out_dtype" in _lib.last_error()
+
+
 def test_workspace_size_is_consistent():
     lib = _lib.load()
     assert lib.du_decode_workspace_size(8, 32, 32, 128, 64) == 0  # one split per row
