@@ -1277,8 +1277,9 @@ int du_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, c
     rc = noalloc_scratch_address(&scratch);
     if (rc != DU_OK) return rc;
   }
-  // Nothing in the scratch needs clearing: the split kernel writes every partial the merge
-  // reads. Calls sharing the array must not overlap on the GPU.
+  // Nothing is cleared here: the split kernel writes every partial before it is read, and the
+  // ticket counters at the start of the array are zero at load and left zero by every call.
+  // Calls sharing the array must not overlap on the GPU.
   return decode_impl(q, k_cache, v_cache, cos, sin, out, nullptr, nullptr, B, Hq, Hkv, L, D,
                      dtype, scale, L, 0, rope_positions, scratch, need,
                      static_cast<cudaStream_t>(stream));

@@ -223,10 +223,12 @@ int du_exchange_merge(const float* o_local, const float* lse_local, void* const*
  * The first call on a device, and the first after its context is re-created (for instance by
  * cudaDeviceReset), looks up that device's address of the array (cudaGetSymbolAddress, with
  * the device current); make that first call before any stream capture. All calls on a device
- * share the one array and nothing in it needs clearing (every partial is written before it is
- * read), so calls that may overlap on the GPU -- on different streams, or from different host
- * threads -- race; serialise them. Calls issued one after the other on one stream do not
- * overlap.
+ * share the one array, which keeps what the last call left: the partials are always written
+ * before they are read, and the ticket counters at its start (with which the tensor-core
+ * decode merges a unit's partials) are zero when the library loads and are returned to zero
+ * by every call, so no call clears anything. Calls that may overlap on the GPU -- on
+ * different streams, or from different host threads -- race on the array; serialise them.
+ * Calls issued one after the other on one stream do not overlap.
  */
 #define DU_NOALLOC_SCRATCH_BYTES (4u << 20)
 int du_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, const void* cos,
