@@ -191,6 +191,8 @@ class PeerExchange:
         from . import _lib
         from .attention import _dtype_code
 
+        if self._own is None:
+            raise RuntimeError("this PeerExchange is closed")
         if o_local.dtype != torch.float32 or lse_local.dtype != torch.float32:
             raise ValueError("partials must be float32")
         o2 = o_local.reshape(-1, self.D)
