@@ -450,6 +450,20 @@ def bench_decode_long(dist, rank, world, device, stream, steps, warmup, peaks):
     for i in range(warmup):
         step(i)
     torch.cuda.synchronize()
+    if ex is not None:
+        # A bounded wait that expired during the warm-up (status code 5 on any rank) means the
+        # peer exchange does not work here: every rank falls back to NCCL before timing.
+        from dominusultra_b200 import _lib as _dlib
+
+        bad = torch.tensor([1 if _dlib.read_status(reset=True)[0] != 0 else 0], device=device)
+        dist.all_reduce(bad, op=dist.ReduceOp.MAX)
+        if int(bad.item()):
+            ex.close()
+            ex = None
+            step = step_nccl
+            for i in range(warmup):
+                step(i)
+            torch.cuda.synchronize()
     barrier(dist)
     # Eagerly launched, the host path of a step (Python wrappers and the collective, ~75 us with
     # NCCL) exceeds the device time of a rank's shard at eight GPUs; a generation loop replays the
