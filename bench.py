@@ -430,7 +430,7 @@ def bench_decode_long(dist, rank, world, device, stream, steps, warmup, peaks):
         try:
             ex = ddist.PeerExchange(rows, D, device=device)
             ok = 1
-        except RuntimeError:
+        except (RuntimeError, ValueError):  # no CUDA IPC here, or more ranks than it supports
             ok = 0
         flag = torch.tensor([ok], device=device)
         dist.all_reduce(flag, op=dist.ReduceOp.MIN)
